@@ -1,0 +1,144 @@
+// Weighted combine (unpermute): one warp per token sums its k expert rows in
+// slot order in f32, adds the shared expert's row, rounds once. 16-byte loads.
+// Also the per-channel int8 quantiser (one warp per weight row).
+#pragma once
+#include "ptx.cuh"
+
+namespace moe {
+namespace combine {
+
+constexpr int kThreads = 256;
+constexpr int kMaxK = 32;
+
+struct Params {
+  const void* y;
+  const void* y_shared;
+  const int32_t* pos;
+  const float* w;
+  void* out;
+  int32_t* status;
+  int64_t T, H;
+  int k, y_dtype, out_dtype;
+};
+
+__device__ __forceinline__ void load8(const void* base, int dt, int64_t off, float (&v)[8]) {
+  if (dt == MOE_DT_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + off);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + off + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + off);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (dt == MOE_DT_BF16) {
+        const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+        v[2 * i] = __low2float(h);
+        v[2 * i + 1] = __high2float(h);
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        v[2 * i] = __low2float(h);
+        v[2 * i + 1] = __high2float(h);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store8(void* base, int dt, int64_t off, const float (&v)[8]) {
+  if (dt == MOE_DT_F32) {
+    float* o = reinterpret_cast<float*>(base) + off;
+    *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (dt == MOE_DT_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base) + off) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) combine_kernel(const Params p) {
+  __shared__ int s_pos[kThreads / 32][kMaxK];
+  __shared__ float s_w[kThreads / 32][kMaxK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp;
+  if (t >= p.T) return;
+  const int64_t rows = p.T * p.k;
+  if (lane < p.k) {
+    int r = p.pos[t * p.k + lane];
+    float w = p.w[t * p.k + lane];
+    if (r < 0 || r >= rows) {
+      // a slot the grouping rejected (or a corrupted position): contributes 0
+      if (p.status && r >= rows) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
+      r = 0;
+      w = 0.f;
+    }
+    s_pos[warp][lane] = r;
+    s_w[warp][lane] = w;
+  }
+  __syncwarp();
+  for (int64_t h = lane * 8; h < p.H; h += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < p.k; ++s) {
+      const int row = s_pos[warp][s];
+      const float ws = s_w[warp][s];
+      float v[8];
+      load8(p.y, p.y_dtype, static_cast<int64_t>(row) * p.H + h, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(ws, v[i], acc[i]);
+    }
+    if (p.y_shared) {
+      float v[8];
+      load8(p.y_shared, p.y_dtype, t * p.H + h, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+    }
+    store8(p.out, p.out_dtype, t * p.H + h, acc);
+  }
+}
+
+struct QuantParams {
+  const void* w;
+  int8_t* q;
+  void* scale;
+  int64_t rows, K;
+  int w_dtype, scale_bf16;
+};
+
+__device__ __forceinline__ float ldf(const void* p, int dt, int64_t i) {
+  if (dt == MOE_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == MOE_DT_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp;
+  if (r >= p.rows) return;
+  const int64_t off = r * p.K;
+  float amax = 0.f;
+  for (int64_t i = lane; i < p.K; i += 32) amax = fmaxf(amax, fabsf(ldf(p.w, p.w_dtype, off + i)));
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+  const float scale = amax == 0.f ? 1.0f : amax / 127.0f;
+  for (int64_t i = lane; i < p.K; i += 32) {
+    float qv = rintf(ldf(p.w, p.w_dtype, off + i) / scale);
+    qv = fminf(127.f, fmaxf(-127.f, qv));
+    p.q[off + i] = static_cast<int8_t>(qv);
+  }
+  if (lane == 0) {
+    if (p.scale_bf16) reinterpret_cast<__nv_bfloat16*>(p.scale)[r] = __float2bfloat16_rn(scale);
+    else reinterpret_cast<float*>(p.scale)[r] = scale;
+  }
+}
+
+}  // namespace combine
+}  // namespace moe

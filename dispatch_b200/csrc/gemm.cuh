@@ -1,0 +1,498 @@
+// Persistent, warp-specialised grouped GEMM on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA) for the routed expert FFN.
+//
+// One launch walks a flat tile space made of up to two "segments" (the routed
+// experts and the shared expert). A segment is a list of row groups (one per
+// expert) over one A matrix, sharing N, K and a stacked (G, N, K) weight. Row
+// offsets of the groups live on the device (written by the grouping kernel), so
+// the tile list is derived in-kernel and the host never synchronises.
+//
+// Tile = 128 rows x 256 MMA columns, K in blocks of 64 (one 128-byte swizzle
+// atom of bf16). In a SwiGLU segment the 256 columns are 128 gate rows and the
+// 128 matching up rows of the weight, and the epilogue writes
+// h = silu(gate) * up for 128 output columns; in a plain segment all 256
+// columns are outputs.
+//
+// Warp roles (256 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+// issues tcgen05.mma from one thread, warps 2-3 dequantise int8 weight tiles to
+// bf16/f16 in shared memory (int8 build only), warps 4-7 drain the
+// double-buffered TMEM accumulator (lane quarter = warp % 4) and store.
+// Every mbarrier wait is bounded (ptx.cuh); on expiry the CTA drains its
+// in-flight copies and MMAs, frees TMEM and returns with MOE_ERR_TIMEOUT in the
+// status word.
+#pragma once
+#include "ptx.cuh"
+
+namespace moe {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int BN = 256;
+constexpr int kThreads = 256;
+constexpr int kMaxGroups = 256;
+constexpr int kMaxSegs = 2;
+constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
+constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr uint32_t Q_BYTES = BN * BK;      // 16 KiB int8 staging
+constexpr uint32_t kTmemCols = 2 * BN;     // two accumulators of 256 f32 columns
+constexpr int kConvThreads = 64;           // warps 2-3
+
+template <bool kInt8>
+struct Config {
+  static constexpr int kStages = kInt8 ? 3 : 4;
+  static constexpr uint32_t kStageBytes = A_BYTES + B_BYTES + (kInt8 ? Q_BYTES : 0);
+};
+
+struct Segment {
+  CUtensorMap map_a;   // 2D {K, rows}, box {64, 128}, 128B swizzle
+  CUtensorMap map_b0;  // 3D {K, N, G}: plain weight, or gate for SwiGLU
+  CUtensorMap map_b1;  // 3D up weight (SwiGLU only)
+  const int32_t* offsets;  // G+1 row offsets on the device; nullptr = dense
+  const void* scale0;      // (G, N) per-channel scales of b0 (int8 only)
+  const void* scale1;      // of b1
+  void* out;               // (rows, ldo)
+  int64_t ldo;
+  int groups;
+  int dense_rows;
+  int n;  // output columns
+  int k;
+  int swiglu;
+  int b_int8;
+  int scale_bf16;
+  int pad_;
+};
+
+struct Params {
+  Segment seg[kMaxSegs];
+  int num_segs;
+  int in_f16;   // A/B element type: 0 bf16, 1 f16 (also the output type)
+  int32_t* status;
+};
+
+struct Ctrl {
+  uint64_t full[4];
+  uint64_t conv[4];
+  uint64_t empty[4];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int seg_tiles[kMaxSegs];
+  int off[kMaxSegs][kMaxGroups + 1];
+  int mt[kMaxSegs][kMaxGroups + 1];
+};
+
+__host__ __device__ constexpr int out_cols_per_tile(int swiglu) { return swiglu ? BN / 2 : BN; }
+
+struct Tile {
+  int seg, group, row0, rows, n_tile;
+};
+
+__device__ __forceinline__ bool decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
+  int s = 0;
+  while (s < p.num_segs && t >= c.seg_tiles[s]) {
+    t -= c.seg_tiles[s];
+    ++s;
+  }
+  if (s >= p.num_segs) return false;
+  const Segment& S = p.seg[s];
+  const int nt = (S.n + out_cols_per_tile(S.swiglu) - 1) / out_cols_per_tile(S.swiglu);
+  int lo = 0, hi = S.groups;  // largest g in [0, G) with mt[g] * nt <= t
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (c.mt[s][mid] * nt <= t) lo = mid; else hi = mid;
+  }
+  const int local = t - c.mt[s][lo] * nt;
+  const int mtg = c.mt[s][lo + 1] - c.mt[s][lo];
+  const int m_tile = local % mtg;
+  tl.seg = s;
+  tl.group = lo;
+  tl.n_tile = local / mtg;
+  tl.row0 = c.off[s][lo] + m_tile * BM;
+  tl.rows = min(BM, c.off[s][lo + 1] - tl.row0);
+  return true;
+}
+
+__device__ __forceinline__ float ld_scale(const void* p, int bf16, int64_t i) {
+  return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
+}
+
+// Stores 32 consecutive f32 values of one output row as bf16/f16.
+__device__ __forceinline__ void store_row32(void* out, int64_t elem_off, const float (&v)[32], int ncols, int f16,
+                                            bool vec_ok) {
+  if (f16) {
+    __half* o = reinterpret_cast<__half*>(out) + elem_off;
+    if (ncols == 32 && vec_ok) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __half2 h0 = __floats2half2_rn(v[q * 8 + 0], v[q * 8 + 1]);
+        __half2 h1 = __floats2half2_rn(v[q * 8 + 2], v[q * 8 + 3]);
+        __half2 h2 = __floats2half2_rn(v[q * 8 + 4], v[q * 8 + 5]);
+        __half2 h3 = __floats2half2_rn(v[q * 8 + 6], v[q * 8 + 7]);
+        w.x = *reinterpret_cast<uint32_t*>(&h0);
+        w.y = *reinterpret_cast<uint32_t*>(&h1);
+        w.z = *reinterpret_cast<uint32_t*>(&h2);
+        w.w = *reinterpret_cast<uint32_t*>(&h3);
+        reinterpret_cast<uint4*>(o)[q] = w;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) o[j] = __float2half_rn(v[j]);
+    }
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + elem_off;
+    if (ncols == 32 && vec_ok) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
+        w.x = *reinterpret_cast<uint32_t*>(&h0);
+        w.y = *reinterpret_cast<uint32_t*>(&h1);
+        w.z = *reinterpret_cast<uint32_t*>(&h2);
+        w.w = *reinterpret_cast<uint32_t*>(&h3);
+        reinterpret_cast<uint4*>(o)[q] = w;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) o[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+// Exact int8 -> 16-bit float for 16 packed bytes. Each signed byte b becomes
+// the f32 2^23 + (b + 128) by byte placement, minus 2^23 + 128.
+__device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+  uint32_t out[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float f[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t bits = __byte_perm(w[i], 0x4B000000u, 0x7540u | static_cast<uint32_t>(b));
+      f[b] = __uint_as_float(bits) - 8388736.0f;
+    }
+    if (f16) {
+      __half2 a = __floats2half2_rn(f[0], f[1]);
+      __half2 c = __floats2half2_rn(f[2], f[3]);
+      out[2 * i] = *reinterpret_cast<uint32_t*>(&a);
+      out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&c);
+    } else {
+      __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]);
+      __nv_bfloat162 c = __floats2bfloat162_rn(f[2], f[3]);
+      out[2 * i] = *reinterpret_cast<uint32_t*>(&a);
+      out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&c);
+    }
+  }
+  lo = make_uint4(out[0], out[1], out[2], out[3]);
+  hi = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+template <bool kInt8>
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+  using Cfg = Config<kInt8>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = sA + S * A_BYTES;
+  uint8_t* sQ = sB + S * B_BYTES;
+  Ctrl& c = *reinterpret_cast<Ctrl*>(sB + S * B_BYTES + (kInt8 ? S * Q_BYTES : 0));
+  volatile int* abort_flag = &c.abort;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---- setup: group offsets and per-group m-tile prefix in shared memory
+  for (int s = 0; s < p.num_segs; ++s) {
+    const Segment& Sg = p.seg[s];
+    for (int g = tid; g <= Sg.groups; g += kThreads)
+      c.off[s][g] = Sg.offsets ? Sg.offsets[g] : (g == 0 ? 0 : Sg.dense_rows);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.conv[i], kConvThreads);
+      mbar_init(&c.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&c.tfull[i], 1);
+      mbar_init(&c.tempty[i], 4 * 32);
+    }
+    mbar_init(&c.drain, 1);
+    c.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&c.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  if (warp < p.num_segs) {
+    const int s = warp;
+    const Segment& Sg = p.seg[s];
+    int running = 0;
+    // Offsets come from another kernel: refuse (and report) a segment whose
+    // offsets are not monotone inside [0, rows] instead of storing out of range.
+    bool bad = lane == 0 && (c.off[s][0] < 0 || c.off[s][Sg.groups] > Sg.dense_rows);
+    if (lane == 0) c.mt[s][0] = 0;
+    for (int g0 = 0; g0 < Sg.groups; g0 += 32) {
+      const int g = g0 + lane;
+      int v = 0;
+      if (g < Sg.groups) {
+        const int rows = c.off[s][g + 1] - c.off[s][g];
+        bad |= rows < 0;
+        v = rows > 0 ? (rows + BM - 1) / BM : 0;
+      }
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += o;
+      }
+      if (g < Sg.groups) c.mt[s][g + 1] = running + v;
+      running += __shfl_sync(0xffffffffu, v, 31);
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 0) {
+      const int nt = (Sg.n + out_cols_per_tile(Sg.swiglu) - 1) / out_cols_per_tile(Sg.swiglu);
+      c.seg_tiles[s] = bad ? 0 : running * nt;
+      if (bad && p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = c.tmem_base;
+  int total = 0;
+  for (int s = 0; s < p.num_segs; ++s) total += c.seg_tiles[s];
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      for (int s = 0; s < p.num_segs; ++s) {
+        tma_prefetch_desc(&p.seg[s].map_a);
+        tma_prefetch_desc(&p.seg[s].map_b0);
+        if (p.seg[s].swiglu) tma_prefetch_desc(&p.seg[s].map_b1);
+      }
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        Tile tl;
+        decode_tile(c, p, t, tl);
+        const Segment& Sg = p.seg[tl.seg];
+        const int nkb = (Sg.k + BK - 1) / BK;
+        const int n0 = tl.n_tile * out_cols_per_tile(Sg.swiglu);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          if (kInt8 && Sg.b_int8) {
+            uint8_t* q_dst = sQ + stage * Q_BYTES;
+            mbar_arrive_expect_tx(&c.full[stage], A_BYTES + Q_BYTES);
+            tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
+            if (Sg.swiglu) {
+              tma_load_3d(q_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
+              tma_load_3d(q_dst + Q_BYTES / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
+            } else {
+              tma_load_3d(q_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
+            }
+          } else {
+            uint8_t* b_dst = sB + stage * B_BYTES;
+            mbar_arrive_expect_tx(&c.full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
+            if (Sg.swiglu) {
+              tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
+              tma_load_3d(b_dst + B_BYTES / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
+            } else {
+              tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
+            }
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // Let every copy this thread started land before the CTA exits.
+        for (int i = 0; i < S; ++i) {
+          if (!(issued_mask & (1u << i))) continue;
+          const uint32_t par = (issued_parity >> i) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&c.full[i], par) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BM, BN, p.in_f16 != 0);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      // conv[s] completes a phase only when an int8 tile uses stage s, so its
+      // parity is tracked per stage, apart from the full/empty phase.
+      uint32_t conv_par = 0;
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        Tile tl;
+        decode_tile(c, p, t, tl);
+        const Segment& Sg = p.seg[tl.seg];
+        const int nkb = (Sg.k + BK - 1) / BK;
+        if (!wait_parity_bounded(&c.tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (kInt8 && Sg.b_int8) {
+            if (!wait_parity_bounded(&c.conv[stage], (conv_par >> stage) & 1u, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            conv_par ^= 1u << stage;
+          } else if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            mma_f16_ss(d, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), idesc,
+                       (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit(&c.empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(&c.tfull[acc]);
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok && issued) {
+        mma_commit(&c.drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&c.drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ int8 -> bf16/f16
+    if constexpr (kInt8) {
+      const int ct = tid - 64;
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        Tile tl;
+        decode_tile(c, p, t, tl);
+        const Segment& Sg = p.seg[tl.seg];
+        const int nkb = (Sg.k + BK - 1) / BK;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (Sg.b_int8) {
+            if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) { ok = false; break; }
+            const uint8_t* q = sQ + stage * Q_BYTES;
+            uint8_t* b = sB + stage * B_BYTES;
+            for (int item = ct; item < BN * 4; item += kConvThreads) {
+              const int r = item >> 2, cc = item & 3;
+              const uint4 v = *reinterpret_cast<const uint4*>(q + r * 64 + cc * 16);
+              uint4 lo, hi;
+              dequant16(v, p.in_f16, lo, hi);
+              uint8_t* row = b + r * 128;
+              *reinterpret_cast<uint4*>(row + (((2 * cc) ^ (r & 7)) << 4)) = lo;
+              *reinterpret_cast<uint4*>(row + (((2 * cc + 1) ^ (r & 7)) << 4)) = hi;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&c.conv[stage]);
+          }
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      Tile tl;
+      decode_tile(c, p, t, tl);
+      const Segment& Sg = p.seg[tl.seg];
+      if (!wait_parity_bounded(&c.tfull[acc], acc_phase, abort_flag, p.status)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const bool valid = r < tl.rows;
+      const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo;
+      const bool vec_ok = (Sg.ldo % 8) == 0;
+      const int64_t sc_base = static_cast<int64_t>(tl.group) * Sg.n;
+      if (Sg.swiglu) {
+        const int n0 = tl.n_tile * (BN / 2);
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tb + ch * 32, gv);
+          tmem_ld_32x32b_x32(tb + BN / 2 + ch * 32, uv);
+          tmem_ld_wait();
+          const int col0 = n0 + ch * 32;
+          if (valid && col0 < Sg.n) {
+            const int nc = min(32, Sg.n - col0);
+            float h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float g = __uint_as_float(gv[j]);
+              float u = __uint_as_float(uv[j]);
+              if (kInt8 && Sg.b_int8 && j < nc) {
+                g *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
+                u *= ld_scale(Sg.scale1, Sg.scale_bf16, sc_base + col0 + j);
+              }
+              h[j] = g / (1.0f + __expf(-g)) * u;
+            }
+            store_row32(Sg.out, row_off + col0, h, nc, p.in_f16, vec_ok);
+          }
+        }
+      } else {
+        const int n0 = tl.n_tile * BN;
+#pragma unroll 1
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tb + ch * 32, v);
+          tmem_ld_wait();
+          const int col0 = n0 + ch * 32;
+          if (valid && col0 < Sg.n) {
+            const int nc = min(32, Sg.n - col0);
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              o[j] = __uint_as_float(v[j]);
+              if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
+            }
+            store_row32(Sg.out, row_off + col0, o, nc, p.in_f16, vec_ok);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&c.tempty[acc]);
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <bool kInt8>
+constexpr size_t smem_bytes() {
+  return 1024 + Config<kInt8>::kStages * Config<kInt8>::kStageBytes + sizeof(Ctrl);
+}
+
+}  // namespace gemm
+}  // namespace moe

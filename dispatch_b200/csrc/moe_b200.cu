@@ -1,0 +1,611 @@
+// Host side of the C ABI declared in include/moe_b200.h: argument checks,
+// TMA tensor-map encoding and kernel launches. No allocation happens here.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/moe_b200.h"
+#include "combine.cuh"
+#include "gemm.cuh"
+#include "group.cuh"
+#include "route.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CUDA_TRY(expr, what)                 \
+  do {                                       \
+    cudaError_t _e = (expr);                 \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+#define CHECK_ARG(cond, ...)                                   \
+  do {                                                         \
+    if (!(cond)) return fail(MOE_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::once_flag once;
+  int sms = 0;
+  int major = 0;
+};
+std::array<DeviceInfo, kMaxDevices> g_dev;
+
+int device_info(int* sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(MOE_ERR_NO_DEVICE, "no CUDA device is current");
+  DeviceInfo& d = g_dev[dev];
+  std::call_once(d.once, [&] {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+  });
+  if (d.major != 10) return fail(MOE_ERR_NO_DEVICE, "device %d is sm_%d0, this library is built for sm_100a", dev, d.major);
+  *sms = d.sms;
+  return MOE_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool is16(int dt) { return dt == MOE_DT_BF16 || dt == MOE_DT_F16; }
+size_t dt_size(int dt) {
+  switch (dt) {
+    case MOE_DT_BF16: case MOE_DT_F16: return 2;
+    case MOE_DT_F32: case MOE_DT_I32: return 4;
+    case MOE_DT_I8: return 1;
+    case MOE_DT_I64: return 8;
+    default: return 0;
+  }
+}
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// A operand: 2D {K, rows} with row stride lda elements, box {64, 128}.
+int make_map_a(CUtensorMap* m, const void* a, int dt, int64_t rows, int64_t K, int64_t lda) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda * 2)};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, dt == MOE_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(a), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MOE_ERR_INVALID_ARG, "tensor map (A) encode failed (%d)", static_cast<int>(r));
+  return MOE_OK;
+}
+
+// B operand: 3D {K, N, G}, box {64, box_rows, 1}; 16-bit types use the
+// 128-byte swizzle, int8 is staged unswizzled for the in-smem dequantiser.
+int make_map_b(CUtensorMap* m, const void* w, int dt, int64_t G, int64_t N, int64_t K, int box_rows) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const size_t es_b = dt_size(dt);
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(G)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(K * es_b), static_cast<cuuint64_t>(N * K * es_b)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUtensorMapDataType t = dt == MOE_DT_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                          : dt == MOE_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(m, t, 3, const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   dt == MOE_DT_I8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MOE_ERR_INVALID_ARG, "tensor map (B) encode failed (%d)", static_cast<int>(r));
+  return MOE_OK;
+}
+
+// Description of one GEMM segment before encoding.
+struct SegSpec {
+  const void* a;
+  int64_t a_rows;
+  int64_t lda;
+  const void* b0;
+  const void* b1;
+  int b_dtype;  // activation type or MOE_DT_I8
+  const void* scale0;
+  const void* scale1;
+  int scale_dtype;
+  int64_t G, N, K;
+  const int32_t* offsets;  // nullptr => dense over a_rows
+  void* out;
+  int64_t ldo;
+  bool swiglu;
+};
+
+int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
+  std::memset(s, 0, sizeof(*s));
+  int rc = make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
+  if (rc) return rc;
+  const int box_rows = sp.swiglu ? moe::gemm::BN / 2 : moe::gemm::BN;
+  rc = make_map_b(&s->map_b0, sp.b0, sp.b_dtype, sp.G, sp.N, sp.K, box_rows);
+  if (rc) return rc;
+  if (sp.swiglu) {
+    rc = make_map_b(&s->map_b1, sp.b1, sp.b_dtype, sp.G, sp.N, sp.K, box_rows);
+    if (rc) return rc;
+  }
+  s->offsets = sp.offsets;
+  s->scale0 = sp.scale0;
+  s->scale1 = sp.scale1;
+  s->out = sp.out;
+  s->ldo = sp.ldo;
+  s->groups = static_cast<int>(sp.offsets ? sp.G : 1);
+  s->dense_rows = static_cast<int>(sp.a_rows);
+  s->n = static_cast<int>(sp.N);
+  s->k = static_cast<int>(sp.K);
+  s->swiglu = sp.swiglu ? 1 : 0;
+  s->b_int8 = sp.b_dtype == MOE_DT_I8 ? 1 : 0;
+  s->scale_bf16 = sp.scale_dtype == MOE_DT_BF16 ? 1 : 0;
+  return MOE_OK;
+}
+
+int check_seg(const SegSpec& sp, int act_dtype) {
+  CHECK_ARG(sp.a && sp.b0 && sp.out, "null operand pointer");
+  CHECK_ARG(!sp.swiglu || sp.b1, "null up-projection pointer");
+  CHECK_ARG(sp.a_rows > 0 && sp.a_rows < (1ll << 31), "row count %lld out of range", (long long)sp.a_rows);
+  CHECK_ARG(sp.G >= 1 && sp.G <= moe::gemm::kMaxGroups, "expert count %lld not in [1, %d]", (long long)sp.G,
+            moe::gemm::kMaxGroups);
+  CHECK_ARG(sp.N >= 1 && sp.N < (1ll << 31) && sp.K >= 1 && sp.K < (1ll << 31), "bad N/K");
+  CHECK_ARG(is16(act_dtype), "activation dtype must be bf16 or f16");
+  CHECK_ARG(sp.b_dtype == act_dtype || sp.b_dtype == MOE_DT_I8, "dtype mismatch: weight %d vs activation %d",
+            sp.b_dtype, act_dtype);
+  const int kmul = sp.b_dtype == MOE_DT_I8 ? 16 : 8;
+  CHECK_ARG(sp.K % kmul == 0, "K mismatch: K=%lld must be a multiple of %d", (long long)sp.K, kmul);
+  CHECK_ARG(sp.lda % 8 == 0 && aligned16(sp.a) && aligned16(sp.b0) && (!sp.b1 || aligned16(sp.b1)),
+            "operands must be 16-byte aligned with row strides a multiple of 16 bytes");
+  if (sp.b_dtype == MOE_DT_I8) {
+    CHECK_ARG(sp.scale0 && (!sp.swiglu || sp.scale1), "int8 weights need scales");
+    CHECK_ARG(sp.scale_dtype == MOE_DT_F32 || sp.scale_dtype == MOE_DT_BF16, "scale dtype must be f32 or bf16");
+  }
+  return MOE_OK;
+}
+
+template <bool kInt8>
+int launch_gemm(const moe::gemm::Params& p, int sms, cudaStream_t stream) {
+  constexpr size_t smem = moe::gemm::smem_bytes<kInt8>();
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_kernel<kInt8>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(gemm)");
+  moe::gemm::grouped_gemm_kernel<kInt8><<<sms, moe::gemm::kThreads, smem, stream>>>(p);
+  CUDA_TRY(cudaGetLastError(), "grouped_gemm_kernel launch");
+  return MOE_OK;
+}
+
+int run_gemm(const SegSpec* specs, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  moe::gemm::Params p;
+  std::memset(&p, 0, sizeof(p));
+  bool any_i8 = false;
+  int64_t tiles_bound = 0;
+  for (int i = 0; i < nseg; ++i) {
+    rc = check_seg(specs[i], act_dtype);
+    if (rc) return rc;
+    rc = fill_segment(&p.seg[i], specs[i], act_dtype);
+    if (rc) return rc;
+    any_i8 |= specs[i].b_dtype == MOE_DT_I8;
+    const int oc = moe::gemm::out_cols_per_tile(specs[i].swiglu);
+    const int64_t mt = (specs[i].a_rows + moe::gemm::BM - 1) / moe::gemm::BM + (specs[i].offsets ? specs[i].G : 0);
+    tiles_bound += mt * ((specs[i].N + oc - 1) / oc);
+  }
+  p.num_segs = nseg;
+  p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
+  p.status = status;
+  const int grid = static_cast<int>(tiles_bound < sms ? tiles_bound : sms);
+  if (grid <= 0) return MOE_OK;
+  return any_i8 ? launch_gemm<true>(p, grid, stream) : launch_gemm<false>(p, grid, stream);
+}
+
+int route_tb(int64_t H, int E, bool computing) {
+  if (!computing) return 16;
+  int tb = 16;
+  while (tb > 1 && static_cast<int64_t>(tb) * (H + E) * 4 > 120 * 1024) tb >>= 1;
+  return tb;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+const char* moe_status_string(int code) {
+  switch (code) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_INVALID_ARG: return "invalid argument";
+    case MOE_ERR_UNSUPPORTED: return "unsupported";
+    case MOE_ERR_CUDA: return "CUDA error";
+    case MOE_ERR_NO_DEVICE: return "no sm_100 device";
+    case MOE_ERR_TIMEOUT: return "device wait timed out";
+    case MOE_ERR_BAD_EXPERT: return "expert id out of range";
+    case MOE_ERR_BAD_OFFSETS: return "group offsets or row positions out of range";
+    default: return "unknown status";
+  }
+}
+
+const char* moe_last_error(void) { return g_last_error.c_str(); }
+
+int moe_device_sm_count(void) {
+  int sms = 0;
+  return device_info(&sms) == MOE_OK ? sms : 0;
+}
+
+int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, const float* logits_in, int64_t T,
+              int64_t H, int64_t E, int k, int mode, int renorm, const float* e_score_bias, int n_group,
+              int topk_group, float routed_scaling, int32_t* topk_idx, float* topk_w, float* logits_out,
+              int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(T >= 0 && E >= 1 && E <= moe::route::kMaxE, "E=%lld must be in [1, %d]", (long long)E, moe::route::kMaxE);
+  CHECK_ARG(k >= 1 && k <= moe::route::kMaxK && k <= E, "top_k=%d must be in [1, min(E, %d)]", k, moe::route::kMaxK);
+  CHECK_ARG(topk_idx && topk_w, "null output pointer");
+  CHECK_ARG(logits_in || (x && router_w && H >= 1), "need logits_in or x and router_w");
+  if (!logits_in) {
+    CHECK_ARG(x_dtype == MOE_DT_BF16 || x_dtype == MOE_DT_F16 || x_dtype == MOE_DT_F32, "bad x dtype");
+    CHECK_ARG(w_dtype == MOE_DT_BF16 || w_dtype == MOE_DT_F16 || w_dtype == MOE_DT_F32, "bad router dtype");
+  }
+  CHECK_ARG(mode == MOE_ROUTER_SOFTMAX || mode == MOE_ROUTER_SIGMOID_GROUP, "unknown router mode %d", mode);
+  if (mode == MOE_ROUTER_SIGMOID_GROUP) {
+    CHECK_ARG(n_group >= 1 && n_group <= 32 && E % n_group == 0, "n_group=%d must divide E and be <= 32", n_group);
+    CHECK_ARG(topk_group >= 1 && topk_group <= n_group, "topk_group=%d not in [1, n_group]", topk_group);
+    CHECK_ARG(static_cast<int64_t>(topk_group) * (E / n_group) >= k, "kept groups hold fewer than top_k experts");
+  }
+  if (T == 0) return MOE_OK;
+  moe::route::Params p;
+  p.x = x;
+  p.w = router_w;
+  p.logits_in = logits_in;
+  p.bias = e_score_bias;
+  p.topk_idx = topk_idx;
+  p.topk_w = topk_w;
+  p.logits_out = logits_out;
+  p.status = status;
+  p.T = T;
+  p.H = H;
+  p.E = static_cast<int>(E);
+  p.k = k;
+  p.mode = mode;
+  p.renorm = renorm;
+  p.n_group = n_group;
+  p.topk_group = topk_group;
+  p.x_dtype = x_dtype;
+  p.w_dtype = w_dtype;
+  p.scaling = routed_scaling;
+  p.tb = route_tb(H, p.E, logits_in == nullptr);
+  const size_t smem = static_cast<size_t>(p.tb) * (p.E + (logits_in ? 0 : H)) * sizeof(float);
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(moe::route::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  });
+  const int64_t grid = (T + p.tb - 1) / p.tb;
+  moe::route::route_kernel<<<static_cast<unsigned>(grid), moe::route::kThreads, smem,
+                             static_cast<cudaStream_t>(stream)>>>(p);
+  CUDA_TRY(cudaGetLastError(), "route_kernel launch");
+  return MOE_OK;
+}
+
+size_t moe_group_workspace_bytes(int64_t T, int k, int64_t E) {
+  const int64_t n = T * k;
+  const int64_t chunks = (n + moe::group::kChunk - 1) / moe::group::kChunk;
+  return static_cast<size_t>((chunks > 0 ? chunks : 1) * E) * sizeof(int32_t);
+}
+
+int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T, int k, int64_t E,
+                     int32_t* counts, int32_t* offsets, int32_t* pos, int64_t* sorted_token_idx,
+                     float* sorted_weight, const void* x, int x_dtype, int64_t H, void* xs, int xs_dtype,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(E >= 1 && E <= moe::group::kMaxE, "E=%lld must be in [1, %d]", (long long)E, moe::group::kMaxE);
+  CHECK_ARG(k >= 1 && T >= 0, "bad T/k");
+  CHECK_ARG(idx_dtype == MOE_DT_I32 || idx_dtype == MOE_DT_I64, "topk_idx must be int32 or int64");
+  CHECK_ARG(counts && offsets && pos, "null output pointer");
+  CHECK_ARG(!sorted_weight || topk_w, "sorted_weight needs topk_w");
+  CHECK_ARG(workspace && workspace_bytes >= moe_group_workspace_bytes(T, k, E), "workspace too small");
+  if (xs) {
+    CHECK_ARG(x && H >= 8 && H % 8 == 0, "gather needs x and H a multiple of 8");
+    CHECK_ARG(is16(xs_dtype), "xs dtype must be bf16 or f16");
+    CHECK_ARG(x_dtype == MOE_DT_F32 || x_dtype == xs_dtype, "x dtype must be f32 or match xs");
+    CHECK_ARG(aligned16(x) && aligned16(xs), "x/xs must be 16-byte aligned");
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = T * k;
+  if (n == 0) {
+    CUDA_TRY(cudaMemsetAsync(counts, 0, E * sizeof(int32_t), s), "memset counts");
+    CUDA_TRY(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), s), "memset offsets");
+    return MOE_OK;
+  }
+  moe::group::Params p;
+  p.idx = topk_idx;
+  p.idx64 = idx_dtype == MOE_DT_I64;
+  p.w = topk_w;
+  p.n = n;
+  p.k = k;
+  p.E = static_cast<int>(E);
+  p.nchunks = static_cast<int>((n + moe::group::kChunk - 1) / moe::group::kChunk);
+  p.counts = counts;
+  p.offsets = offsets;
+  p.pos = pos;
+  p.sorted_token_idx = sorted_token_idx;
+  p.sorted_weight = sorted_weight;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.H = H;
+  p.xs = xs;
+  p.xs_f16 = xs_dtype == MOE_DT_F16;
+  p.hist = static_cast<int32_t*>(workspace);
+  p.status = status;
+  moe::group::group_hist_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
+  CUDA_TRY(cudaGetLastError(), "group_hist_kernel launch");
+  moe::group::group_scatter_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
+  CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
+  return MOE_OK;
+}
+
+int moe_grouped_gemm(const void* a, int a_dtype, int64_t M, int64_t K, const void* w, int w_dtype,
+                     const void* scale, int scale_dtype, int64_t E, int64_t N, const int32_t* offsets, void* out,
+                     int64_t ldo, int32_t* status, void* stream) {
+  CHECK_ARG(offsets, "null group offsets");
+  if (M == 0) return MOE_OK;
+  CHECK_ARG(ldo >= N, "ldo < N");
+  SegSpec sp{};
+  sp.a = a;
+  sp.a_rows = M;
+  sp.lda = K;
+  sp.b0 = w;
+  sp.b_dtype = w_dtype;
+  sp.scale0 = scale;
+  sp.scale_dtype = scale_dtype;
+  sp.G = E;
+  sp.N = N;
+  sp.K = K;
+  sp.offsets = offsets;
+  sp.out = out;
+  sp.ldo = ldo;
+  sp.swiglu = false;
+  return run_gemm(&sp, 1, a_dtype, status, static_cast<cudaStream_t>(stream));
+}
+
+size_t moe_ffn_workspace_bytes(int64_t R, int64_t I, int64_t T_shared, int64_t I_shared) {
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  return up(static_cast<size_t>(R) * I * 2) + up(static_cast<size_t>(T_shared) * I_shared * 2);
+}
+
+int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
+                        int64_t E, int64_t I, const void* gate, const void* up, const void* down, int w_dtype,
+                        const void* gate_scale, const void* up_scale, const void* down_scale, int scale_dtype,
+                        const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
+                        const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
+                        size_t workspace_bytes, int32_t* status, void* stream) {
+  CHECK_ARG(part >= 1 && part <= 3, "part must be 1 (gate/up), 2 (down) or 3 (both)");
+  const bool has_shared = T_shared > 0 && x_shared;
+  CHECK_ARG(workspace && workspace_bytes >= moe_ffn_workspace_bytes(R, I, has_shared ? T_shared : 0, I_shared),
+            "workspace too small");
+  CHECK_ARG(R == 0 || offsets, "null group offsets");
+  if (has_shared) CHECK_ARG(shared_gate && shared_up && shared_down && y_shared && I_shared > 0, "shared expert args");
+  auto up256 = [](size_t b) { return (b + 255) & ~size_t(255); };
+  void* h = workspace;
+  void* hs = static_cast<char*>(workspace) + up256(static_cast<size_t>(R) * I * 2);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SegSpec g1[2];
+  SegSpec g2[2];
+  int n = 0;
+  if (R > 0) {
+    SegSpec a{};
+    a.a = xs; a.a_rows = R; a.lda = H; a.b0 = gate; a.b1 = up; a.b_dtype = w_dtype; a.scale0 = gate_scale;
+    a.scale1 = up_scale; a.scale_dtype = scale_dtype; a.G = E; a.N = I; a.K = H; a.offsets = offsets; a.out = h;
+    a.ldo = I; a.swiglu = true;
+    SegSpec b{};
+    b.a = h; b.a_rows = R; b.lda = I; b.b0 = down; b.b_dtype = w_dtype; b.scale0 = down_scale;
+    b.scale_dtype = scale_dtype; b.G = E; b.N = H; b.K = I; b.offsets = offsets; b.out = y; b.ldo = H;
+    b.swiglu = false;
+    g1[n] = a;
+    g2[n] = b;
+    ++n;
+  }
+  if (has_shared) {
+    SegSpec a{};
+    a.a = x_shared; a.a_rows = T_shared; a.lda = H; a.b0 = shared_gate; a.b1 = shared_up; a.b_dtype = act_dtype;
+    a.G = 1; a.N = I_shared; a.K = H; a.offsets = nullptr; a.out = hs; a.ldo = I_shared; a.swiglu = true;
+    SegSpec b{};
+    b.a = hs; b.a_rows = T_shared; b.lda = I_shared; b.b0 = shared_down; b.b_dtype = act_dtype; b.G = 1;
+    b.N = H; b.K = I_shared; b.offsets = nullptr; b.out = y_shared; b.ldo = H; b.swiglu = false;
+    g1[n] = a;
+    g2[n] = b;
+    ++n;
+  }
+  if (n == 0) return MOE_OK;
+  if (part & 1) {
+    int rc = run_gemm(g1, n, act_dtype, status, s);
+    if (rc) return rc;
+  }
+  return (part & 2) ? run_gemm(g2, n, act_dtype, status, s) : MOE_OK;
+}
+
+int moe_expert_ffn(const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets, int64_t E,
+                   int64_t I, const void* gate, const void* up, const void* down, int w_dtype,
+                   const void* gate_scale, const void* up_scale, const void* down_scale, int scale_dtype,
+                   const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
+                   const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream) {
+  return moe_expert_ffn_part(3, xs, act_dtype, R, H, offsets, E, I, gate, up, down, w_dtype, gate_scale, up_scale,
+                             down_scale, scale_dtype, x_shared, T_shared, I_shared, shared_gate, shared_up,
+                             shared_down, y, y_shared, workspace, workspace_bytes, status, stream);
+}
+
+int moe_combine(const void* y, int y_dtype, const int32_t* pos, const float* topk_w, int64_t T, int k,
+                int64_t H, const void* y_shared, void* out, int out_dtype, int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(k >= 1 && k <= moe::combine::kMaxK, "top_k=%d must be in [1, %d]", k, moe::combine::kMaxK);
+  CHECK_ARG(H % 8 == 0, "H=%lld must be a multiple of 8", (long long)H);
+  CHECK_ARG(y_dtype == MOE_DT_BF16 || y_dtype == MOE_DT_F16 || y_dtype == MOE_DT_F32, "bad y dtype");
+  CHECK_ARG(out_dtype == MOE_DT_BF16 || out_dtype == MOE_DT_F16 || out_dtype == MOE_DT_F32, "bad out dtype");
+  CHECK_ARG(out && (T == 0 || (y && pos && topk_w)), "null pointer");
+  CHECK_ARG(aligned16(y) && aligned16(out) && aligned16(y_shared), "y/out must be 16-byte aligned");
+  if (T == 0) return MOE_OK;
+  moe::combine::Params p;
+  p.y = y;
+  p.y_shared = y_shared;
+  p.pos = pos;
+  p.w = topk_w;
+  p.out = out;
+  p.T = T;
+  p.H = H;
+  p.k = k;
+  p.y_dtype = y_dtype;
+  p.out_dtype = out_dtype;
+  p.status = status;
+  const int64_t per = moe::combine::kThreads / 32;
+  moe::combine::combine_kernel<<<static_cast<unsigned>((T + per - 1) / per), moe::combine::kThreads, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(p);
+  CUDA_TRY(cudaGetLastError(), "combine_kernel launch");
+  return MOE_OK;
+}
+
+int moe_quantize_int8(const void* w, int w_dtype, int64_t rows, int64_t K, int8_t* q, void* scale,
+                      int scale_dtype, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(w && q && scale, "null pointer");
+  CHECK_ARG(w_dtype == MOE_DT_BF16 || w_dtype == MOE_DT_F16 || w_dtype == MOE_DT_F32, "bad weight dtype");
+  CHECK_ARG(scale_dtype == MOE_DT_F32 || scale_dtype == MOE_DT_BF16, "bad scale dtype");
+  if (rows == 0 || K == 0) return MOE_OK;
+  moe::combine::QuantParams p;
+  p.w = w;
+  p.q = q;
+  p.scale = scale;
+  p.rows = rows;
+  p.K = K;
+  p.w_dtype = w_dtype;
+  p.scale_bf16 = scale_dtype == MOE_DT_BF16;
+  const int64_t per = moe::combine::kThreads / 32;
+  moe::combine::quantize_kernel<<<static_cast<unsigned>((rows + per - 1) / per), moe::combine::kThreads, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(p);
+  CUDA_TRY(cudaGetLastError(), "quantize_kernel launch");
+  return MOE_OK;
+}
+
+// ------------------------------------------------------------------ layer
+namespace {
+struct LayerWs {
+  size_t idx, w, counts, offsets, pos, xs, y, ys, group, ffn, total;
+};
+LayerWs layer_ws(const MoeLayerDesc* d) {
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  LayerWs l{};
+  const size_t T = static_cast<size_t>(d->T), R = T * d->k;
+  const bool shared = d->I_shared > 0;
+  size_t o = 0;
+  l.idx = o; o += up(R * 4);
+  l.w = o; o += up(R * 4);
+  l.counts = o; o += up(static_cast<size_t>(d->E) * 4);
+  l.offsets = o; o += up(static_cast<size_t>(d->E + 1) * 4);
+  l.pos = o; o += up(R * 4);
+  l.xs = o; o += up(R * d->H * 2);
+  l.y = o; o += up(R * d->H * 2);
+  l.ys = o; o += shared ? up(T * d->H * 2) : 0;
+  l.group = o; o += up(moe_group_workspace_bytes(d->T, d->k, d->E));
+  l.ffn = o; o += up(moe_ffn_workspace_bytes(static_cast<int64_t>(R), d->I, shared ? d->T : 0, d->I_shared));
+  l.total = o;
+  return l;
+}
+}  // namespace
+
+size_t moe_layer_workspace_bytes(const MoeLayerDesc* d) { return d ? layer_ws(d).total : 0; }
+
+int moe_layer_forward(const MoeLayerDesc* d, const void* x, const void* router_w, const float* e_score_bias,
+                      const int32_t* topk_idx_in, const float* topk_w_in, const void* gate, const void* up,
+                      const void* down, const void* gate_scale, const void* up_scale, const void* down_scale,
+                      const void* shared_gate, const void* shared_up, const void* shared_down, void* out,
+                      int32_t* topk_idx, float* topk_w, int32_t* counts, int32_t* offsets, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream) {
+  CHECK_ARG(d && x && out, "null pointer");
+  CHECK_ARG(is16(d->act_dtype), "act dtype must be bf16 or f16");
+  CHECK_ARG(d->x_dtype == d->act_dtype || d->x_dtype == MOE_DT_F32, "x dtype must be f32 or the act dtype");
+  const LayerWs l = layer_ws(d);
+  CHECK_ARG(workspace && workspace_bytes >= l.total, "workspace too small (%zu < %zu)", workspace_bytes, l.total);
+  if (d->T == 0) return MOE_OK;
+  char* ws = static_cast<char*>(workspace);
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + l.idx);
+  float* wts = topk_w ? topk_w : reinterpret_cast<float*>(ws + l.w);
+  int32_t* cnt = counts ? counts : reinterpret_cast<int32_t*>(ws + l.counts);
+  int32_t* off = offsets ? offsets : reinterpret_cast<int32_t*>(ws + l.offsets);
+  int32_t* pos = reinterpret_cast<int32_t*>(ws + l.pos);
+  void* xs = ws + l.xs;
+  void* y = ws + l.y;
+  void* ys = d->I_shared > 0 ? ws + l.ys : nullptr;
+  int rc;
+  if (topk_idx_in) {
+    CHECK_ARG(topk_w_in, "topk_w_in missing");
+    idx = const_cast<int32_t*>(topk_idx_in);
+    wts = const_cast<float*>(topk_w_in);
+  } else {
+    rc = moe_route(x, d->x_dtype, router_w, d->router_w_dtype, nullptr, d->T, d->H, d->E, d->k, d->router_mode,
+                   d->renorm, e_score_bias, d->n_group, d->topk_group, d->routed_scaling, idx, wts, nullptr, status,
+                   stream);
+    if (rc) return rc;
+  }
+  rc = moe_group_tokens(idx, MOE_DT_I32, wts, d->T, d->k, d->E, cnt, off, pos, nullptr, nullptr, x, d->x_dtype,
+                        d->H, xs, d->act_dtype, ws + l.group, moe_group_workspace_bytes(d->T, d->k, d->E), status,
+                        stream);
+  if (rc) return rc;
+  // The shared expert reads x directly; an f32 x was converted into xs rows
+  // only, so the shared expert needs x in the activation type.
+  const bool shared = d->I_shared > 0;
+  CHECK_ARG(!shared || d->x_dtype == d->act_dtype, "the shared expert needs x in the activation dtype");
+  rc = moe_expert_ffn(xs, d->act_dtype, d->T * d->k, d->H, off, d->E, d->I, gate, up, down, d->w_dtype, gate_scale,
+                      up_scale, down_scale, d->scale_dtype, shared ? x : nullptr, shared ? d->T : 0, d->I_shared,
+                      shared_gate, shared_up, shared_down, y, ys, ws + l.ffn,
+                      moe_ffn_workspace_bytes(d->T * d->k, d->I, shared ? d->T : 0, d->I_shared), status, stream);
+  if (rc) return rc;
+  return moe_combine(y, d->act_dtype, pos, wts, d->T, d->k, d->H, ys, out, d->out_dtype, status, stream);
+}
+
+}  // extern "C"

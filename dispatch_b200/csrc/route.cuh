@@ -1,0 +1,245 @@
+// Router: logits (x @ router_w^T, f32 accumulate) and expert selection in one
+// kernel. A CTA stages TB token rows of x in shared memory as f32 and each warp
+// walks a strided set of experts, streaming that expert's router row once for
+// all TB tokens; then one warp per token runs the selection:
+//   softmax mode: max, sum of exp, k rounds of warp arg-max (lower id wins a
+//   tie), weight = exp(l - max) / sum, optional renormalisation;
+//   sigmoid-group mode (DeepSeek-V3): s = sigmoid(l), c = s + bias, group
+//   score = top1 + top2 of c in each group, keep topk_group groups, k rounds
+//   of arg-max of c inside them, weight = s (normalised, scaled).
+#pragma once
+#include "ptx.cuh"
+
+namespace moe {
+namespace route {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxE = 256;
+constexpr int kMaxK = 16;
+constexpr int kMaxTB = 16;
+
+struct Params {
+  const void* x;
+  const void* w;
+  const float* logits_in;
+  const float* bias;
+  int32_t* topk_idx;
+  float* topk_w;
+  float* logits_out;
+  int32_t* status;
+  int64_t T, H;
+  int E, k, mode, renorm, n_group, topk_group, x_dtype, w_dtype, tb;
+  float scaling;
+};
+
+__device__ __forceinline__ float to_f32(const void* p, int dt, int64_t i) {
+  if (dt == MOE_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == MOE_DT_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+// Warp arg-max: larger value wins, equal values go to the lower index.
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, d);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, d);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  return v;
+}
+
+__global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
+  extern __shared__ float smem_f[];
+  const int tb = p.tb;
+  const int E = p.E;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tb;
+  const int ntok = static_cast<int>((p.T - t0) < tb ? (p.T - t0) : tb);
+  float* lg = smem_f;                 // [tb][E] logits
+  float* xs = smem_f + tb * E;        // [tb][H] x rows (compute mode)
+  __shared__ float cbuf[kWarps][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (p.logits_in) {
+    for (int i = threadIdx.x; i < ntok * E; i += kThreads) lg[i] = p.logits_in[t0 * E + i];
+  } else {
+    const int64_t H = p.H;
+    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(ntok) * H; i += kThreads)
+      xs[i] = to_f32(p.x, p.x_dtype, t0 * H + i);
+    __syncthreads();
+    for (int e = warp; e < E; e += kWarps) {
+      float acc[kMaxTB];
+#pragma unroll
+      for (int t = 0; t < kMaxTB; ++t) acc[t] = 0.f;
+      for (int64_t h = lane; h < H; h += 32) {
+        const float wv = to_f32(p.w, p.w_dtype, static_cast<int64_t>(e) * H + h);
+#pragma unroll
+        for (int t = 0; t < kMaxTB; ++t)
+          if (t < ntok) acc[t] = fmaf(xs[t * H + h], wv, acc[t]);
+      }
+#pragma unroll
+      for (int t = 0; t < kMaxTB; ++t) {
+        if (t < ntok) {
+          const float s = warp_sum(acc[t]);
+          if (lane == 0) lg[t * E + e] = s;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (p.mode == MOE_ROUTER_SOFTMAX && p.bias) {
+    // softmax mode: the bias is part of the logits (a gate Linear with bias)
+    for (int i = threadIdx.x; i < ntok * E; i += kThreads) lg[i] += p.bias[i % E];
+    __syncthreads();
+  }
+  if (p.logits_out)
+    for (int i = threadIdx.x; i < ntok * E; i += kThreads) p.logits_out[t0 * E + i] = lg[i];
+
+  constexpr int J = kMaxE / 32;
+  for (int t = warp; t < ntok; t += kWarps) {
+    const float* l = lg + t * E;
+    float v[J];
+    int sel[kMaxK];
+    float wsel[kMaxK];
+    if (p.mode == MOE_ROUTER_SOFTMAX) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = e < E ? l[e] : -INFINITY;
+      }
+      float m = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < J; ++j) m = fmaxf(m, v[j]);
+      m = warp_max(m);
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j)
+        if (lane + 32 * j < E) s += expf(v[j] - m);
+      s = warp_sum(s);
+      for (int q = 0; q < p.k; ++q) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          const int e = lane + 32 * j;
+          if (e < E && (v[j] > bv || (v[j] == bv && e < bi))) {
+            bv = v[j];
+            bi = e;
+          }
+        }
+        warp_argmax(bv, bi);
+        sel[q] = bi;
+        wsel[q] = expf(l[bi] - m) / s;
+        if ((bi & 31) == lane) {
+#pragma unroll
+          for (int j = 0; j < J; ++j)
+            if (lane + 32 * j == bi) v[j] = -INFINITY;
+        }
+      }
+      if (p.renorm) {
+        float tot = 0.f;
+        for (int q = 0; q < p.k; ++q) tot += wsel[q];
+        for (int q = 0; q < p.k; ++q) wsel[q] = wsel[q] / tot;
+      }
+    } else {
+      // sigmoid, group-limited
+      float* cb = cbuf[warp];
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) {
+          const float sg = 1.0f / (1.0f + expf(-l[e]));
+          cb[e] = sg + (p.bias ? p.bias[e] : 0.f);
+        }
+      }
+      __syncwarp();
+      const int G = p.n_group, per = E / G;
+      float gs = -INFINITY;
+      if (lane < G) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+        for (int i = 0; i < per; ++i) {
+          const float c = cb[lane * per + i];
+          if (c > b1) {
+            b2 = b1;
+            b1 = c;
+          } else if (c > b2) {
+            b2 = c;
+          }
+        }
+        gs = per >= 2 ? b1 + b2 : b1;
+      }
+      uint32_t gmask = 0;
+      for (int q = 0; q < p.topk_group; ++q) {
+        float bv = (lane < G && !((gmask >> lane) & 1u)) ? gs : -INFINITY;
+        int bi = lane < G && !((gmask >> lane) & 1u) ? lane : 0x7fffffff;
+        warp_argmax(bv, bi);
+        if (bi < 32) gmask |= 1u << bi;
+      }
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = (e < E && ((gmask >> (e / per)) & 1u)) ? cb[e] : -INFINITY;
+      }
+      for (int q = 0; q < p.k; ++q) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          const int e = lane + 32 * j;
+          if (e < E && v[j] != -INFINITY && (v[j] > bv || (v[j] == bv && e < bi))) {
+            bv = v[j];
+            bi = e;
+          }
+        }
+        warp_argmax(bv, bi);
+        sel[q] = bi;
+        wsel[q] = 1.0f / (1.0f + expf(-l[bi]));
+        if ((bi & 31) == lane) {
+#pragma unroll
+          for (int j = 0; j < J; ++j)
+            if (lane + 32 * j == bi) v[j] = -INFINITY;
+        }
+      }
+      if (p.renorm) {
+        float tot = 0.f;
+        for (int q = 0; q < p.k; ++q) tot += wsel[q];
+        for (int q = 0; q < p.k; ++q) wsel[q] = wsel[q] / tot;
+      }
+      for (int q = 0; q < p.k; ++q) wsel[q] *= p.scaling;
+      __syncwarp();
+    }
+    if (lane < p.k) {
+      int si = 0;
+      float sw = 0.f;
+      for (int q = 0; q < p.k; ++q)
+        if (q == lane) {
+          si = sel[q];
+          sw = wsel[q];
+        }
+      if (si < 0 || si >= E) {
+        if (p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_EXPERT);
+        si = 0;
+      }
+      p.topk_idx[(t0 + t) * p.k + lane] = si;
+      p.topk_w[(t0 + t) * p.k + lane] = sw;
+    }
+  }
+}
+
+}  // namespace route
+}  // namespace moe

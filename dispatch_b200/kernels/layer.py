@@ -1,0 +1,147 @@
+"""The whole MoE layer in one C-ABI call: router -> grouping + gather ->
+expert FFN (routed + shared) -> combine, five launches, no host sync.
+
+Mirrors ReferenceMoE.forward (src/dispatch/kernels/reference_moe.py:74-78)
+and adds the routers the BASELINE configs need: renormalised softmax top-k
+(``renormalize=True``) and the DeepSeek-V3 group-limited sigmoid router.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from dispatch_b200 import _lib as L
+from dispatch_b200.kernels.moe_forward import SharedExpertWeights, StackedExpertWeights, act_dtype_for
+from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights
+
+
+@dataclass(frozen=True)
+class RouterConfig:
+    top_k: int
+    mode: str = "softmax"  # "softmax" | "sigmoid_group"
+    renormalize: bool = False
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+
+
+@dataclass(frozen=True)
+class LayerOutput:
+    out: torch.Tensor
+    topk_idx: torch.Tensor  # (T, k) int32
+    topk_weight: torch.Tensor  # (T, k) f32
+    group_sizes: torch.Tensor  # (E,) int32
+    group_offsets: torch.Tensor  # (E+1,) int32
+
+
+def moe_layer_forward(
+    x: torch.Tensor,
+    router_weight: torch.Tensor | None,
+    weights: StackedExpertWeights | QuantizedStackedExpertWeights,
+    router: RouterConfig,
+    *,
+    shared: SharedExpertWeights | None = None,
+    e_score_bias: torch.Tensor | None = None,
+    topk: tuple[torch.Tensor, torch.Tensor] | None = None,
+    out_dtype: torch.dtype | None = None,
+) -> LayerOutput:
+    """x (T, H) bf16/f16 (or f32 with bf16 weights and no shared expert);
+    router_weight (E, H) bf16/f32; ``topk`` = (idx int32 (T,k), w f32 (T,k))
+    skips the router (the moe_infer contract)."""
+    quant = isinstance(weights, QuantizedStackedExpertWeights)
+    g = weights.gate.data if quant else weights.gate
+    u = weights.up.data if quant else weights.up
+    dn = weights.down.data if quant else weights.down
+    dev = L.require_cuda(x, router_weight, g, u, dn, e_score_bias, what="moe_layer_forward")
+    act = act_dtype_for(x, weights)
+    t, h = x.shape
+    e, i, _ = g.shape
+    k = router.top_k
+    x = x.contiguous()
+    desc = L.MoeLayerDesc()
+    desc.T, desc.H, desc.E, desc.I = t, h, e, i
+    desc.I_shared = 0 if shared is None else shared.gate.shape[0]
+    desc.k = k
+    desc.act_dtype = L.dt(act)
+    desc.x_dtype = L.dt(x)
+    desc.out_dtype = L.dt(out_dtype or x.dtype)
+    desc.w_dtype = L.DT_I8 if quant else L.dt(g)
+    desc.scale_dtype = L.dt(weights.gate.scale) if quant else L.DT_F32
+    desc.router_mode = L.ROUTER_SIGMOID_GROUP if router.mode == "sigmoid_group" else L.ROUTER_SOFTMAX
+    desc.renorm = int(router.renormalize)
+    desc.n_group = router.n_group
+    desc.topk_group = router.topk_group
+    desc.routed_scaling = router.routed_scaling_factor
+    desc.router_w_dtype = L.dt(router_weight) if router_weight is not None else L.DT_BF16
+    lib = L.lib()
+    nbytes = lib.moe_layer_workspace_bytes(ctypes.byref(desc))
+    ws = L.workspace(dev, nbytes, "layer")
+    out = torch.empty(t, h, dtype=out_dtype or x.dtype, device=dev)
+    if topk is not None:
+        idx = topk[0].to(torch.int32).contiguous()
+        wts = topk[1].to(torch.float32).contiguous()
+        idx_in, w_in = idx, wts
+    else:
+        idx = torch.empty(t, k, dtype=torch.int32, device=dev)
+        wts = torch.empty(t, k, dtype=torch.float32, device=dev)
+        idx_in = w_in = None
+    counts = torch.empty(e, dtype=torch.int32, device=dev)
+    offsets = torch.empty(e + 1, dtype=torch.int32, device=dev)
+    rw = None if router_weight is None else router_weight.contiguous()
+    sc = (weights.gate.scale, weights.up.scale, weights.down.scale) if quant else (None, None, None)
+    rc = lib.moe_layer_forward(
+        ctypes.byref(desc), x.data_ptr(), L.ptr(rw), L.ptr(e_score_bias),
+        L.ptr(idx_in), L.ptr(w_in),
+        g.contiguous().data_ptr(), u.contiguous().data_ptr(), dn.contiguous().data_ptr(),
+        L.ptr(sc[0]), L.ptr(sc[1]), L.ptr(sc[2]),
+        L.ptr(None if shared is None else shared.gate), L.ptr(None if shared is None else shared.up),
+        L.ptr(None if shared is None else shared.down),
+        out.data_ptr(), None if topk is not None else idx.data_ptr(), None if topk is not None else wts.data_ptr(),
+        counts.data_ptr(), offsets.data_ptr(), ws.data_ptr(), ws.numel(), L.status_word(dev).data_ptr(),
+        L.stream_ptr(dev),
+    )
+    L.check(rc, "moe_layer_forward")
+    return LayerOutput(out, idx, wts, counts, offsets)
+
+
+def route(
+    x: torch.Tensor | None,
+    router_weight: torch.Tensor | None,
+    router: RouterConfig,
+    *,
+    logits: torch.Tensor | None = None,
+    e_score_bias: torch.Tensor | None = None,
+    return_logits: bool = False,
+):
+    """Router only: (topk_idx int32 (T,k), topk_weight f32 (T,k)[, logits f32]).
+    With ``logits`` given the selection runs on exactly those values (the
+    parity boundary "same logits in -> same ids out")."""
+    ref = logits if logits is not None else x
+    dev = L.require_cuda(ref, router_weight if logits is None else None, e_score_bias, what="route")
+    if logits is not None:
+        logits = logits.contiguous().float()
+        t, e = logits.shape
+        h = 0
+    else:
+        t, h = x.shape
+        e = router_weight.shape[0]
+        x = x.contiguous()
+        router_weight = router_weight.contiguous()
+    k = router.top_k
+    idx = torch.empty(t, k, dtype=torch.int32, device=dev)
+    w = torch.empty(t, k, dtype=torch.float32, device=dev)
+    lg = torch.empty(t, e, dtype=torch.float32, device=dev) if return_logits else None
+    bias = None if e_score_bias is None else e_score_bias.contiguous().float()
+    rc = L.lib().moe_route(
+        None if logits is not None else x.data_ptr(), 0 if logits is not None else L.dt(x),
+        None if logits is not None else router_weight.data_ptr(), 0 if logits is not None else L.dt(router_weight),
+        L.ptr(logits), t, h, e, k,
+        L.ROUTER_SIGMOID_GROUP if router.mode == "sigmoid_group" else L.ROUTER_SOFTMAX,
+        int(router.renormalize), L.ptr(bias), router.n_group, router.topk_group, router.routed_scaling_factor,
+        idx.data_ptr(), w.data_ptr(), L.ptr(lg), L.status_word(dev).data_ptr(), L.stream_ptr(dev),
+    )
+    L.check(rc, "route")
+    return (idx, w, lg) if return_logits else (idx, w)

@@ -1,0 +1,204 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Every entry point takes raw device pointers, element counts and a CUDA
+ * stream (as void*), enqueues its kernels on that stream and returns
+ * MOE_OK or a MOE_ERR_* code. Nothing throws across the ABI and nothing
+ * allocates: the caller owns every buffer, including workspaces sized by the
+ * *_workspace_bytes() helpers. Errors found on the device (an expert id out
+ * of range, a bounded wait that expired) are written to a caller-provided
+ * int32 status word in device memory (first error wins; 0 = OK); the caller
+ * reads it after synchronising. Calls are stream-ordered and thread-compatible:
+ * one stream per call, no global mutable state apart from a per-device cache
+ * of the SM count and the driver's tensor-map encoder.
+ *
+ * Layouts (row-major, contiguous unless a leading dimension is passed):
+ *   x            (T, H)        activations, bf16 / f16 / f32
+ *   router_w     (E, H)        bf16 / f32
+ *   gate, up     (E, I, H)     bf16 / f16, or int8 + per-channel scale (E, I)
+ *   down         (E, H, I)     bf16 / f16, or int8 + scale (E, H)
+ *   topk_idx     (T, k) int32, topk_w (T, k) f32
+ *   group offsets (E + 1) int32 exclusive prefix sum of per-expert counts
+ *   pos          (T * k) int32: grouped row of flat slot t*k+s
+ *
+ * Each entry point names the reference function it replaces
+ * (bsreecharanreddy/dispatch, path relative to the project root).
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+/* status codes */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG 1   /* shapes, dtypes, alignment, null pointers */
+#define MOE_ERR_UNSUPPORTED 2   /* a valid request this build does not implement */
+#define MOE_ERR_CUDA 3          /* a CUDA runtime / driver call failed */
+#define MOE_ERR_NO_DEVICE 4     /* no sm_100 device current */
+#define MOE_ERR_TIMEOUT 5       /* device: a bounded wait expired (status word) */
+#define MOE_ERR_BAD_EXPERT 6    /* device: an expert id outside [0, E) (status word) */
+#define MOE_ERR_BAD_OFFSETS 7   /* device: group offsets / row positions out of range (status word) */
+
+/* element types */
+#define MOE_DT_BF16 0
+#define MOE_DT_F16 1
+#define MOE_DT_F32 2
+#define MOE_DT_I8 3
+#define MOE_DT_I32 4
+#define MOE_DT_I64 5
+
+/* router modes */
+#define MOE_ROUTER_SOFTMAX 0        /* softmax top-k (optionally renormalised) */
+#define MOE_ROUTER_SIGMOID_GROUP 1  /* DeepSeek-V3 group-limited sigmoid top-k */
+
+int moe_abi_version(void);
+const char* moe_status_string(int code);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* moe_last_error(void);
+/* Number of SMs of the current device (0 if none). */
+int moe_device_sm_count(void);
+
+/*
+ * Router. Replaces ReferenceMoE.route (src/dispatch/kernels/reference_moe.py:56-61):
+ * logits = x @ router_w^T (fp32 accumulate), then for MOE_ROUTER_SOFTMAX the
+ * fp32 softmax and its top-k (ties to the lower expert id, slots in
+ * descending order), renormalised to sum 1 when renorm != 0 (e_score_bias,
+ * if non-NULL, is added to the logits first: a gate with bias); for
+ * MOE_ROUTER_SIGMOID_GROUP the group-limited sigmoid selection with
+ * e_score_bias (E floats, may be NULL), n_group / topk_group, renorm and
+ * routed_scaling. When logits_in is non-NULL it is used instead of x/router_w
+ * (x and router_w may then be NULL). logits_out (T, E) f32 may be NULL.
+ */
+int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, const float* logits_in, int64_t T,
+              int64_t H, int64_t E, int k, int mode, int renorm, const float* e_score_bias, int n_group,
+              int topk_group, float routed_scaling, int32_t* topk_idx, float* topk_w, float* logits_out,
+              int32_t* status, void* stream);
+
+/*
+ * Token grouping. Replaces group_tokens_by_expert
+ * (src/dispatch/kernels/grouping.py:25-41) and the host-side prefix sum of
+ * build_tile_schedule (src/dispatch/kernels/tile_schedule.py:28-50): a stable
+ * counting sort of the T*k flat (token, slot) pairs by expert, entirely on the
+ * device (no host sync). Outputs: counts (E) int32, offsets (E+1) int32,
+ * pos (T*k) int32; optional (NULL to skip): sorted_token_idx (T*k) int64,
+ * sorted_weight (T*k) f32 (needs topk_w), and the row gather
+ * xs[pos[f]] = x[f / k] (xs (T*k, H) in xs_dtype, bf16 or f16; x in x_dtype).
+ * topk_idx is int32 or int64 (idx_dtype). workspace: moe_group_workspace_bytes
+ * (per-chunk histograms; needs no initialisation). A slot whose id is out of
+ * range gets pos = -1 and MOE_ERR_BAD_EXPERT in the status word.
+ */
+size_t moe_group_workspace_bytes(int64_t T, int k, int64_t E);
+int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T, int k, int64_t E,
+                     int32_t* counts, int32_t* offsets, int32_t* pos, int64_t* sorted_token_idx,
+                     float* sorted_weight, const void* x, int x_dtype, int64_t H, void* xs, int xs_dtype,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Grouped GEMM, the GroupedMatmul contract (src/dispatch/kernels/moe_forward.py:21,
+ * grouped_matmul at src/dispatch/kernels/grouped_gemm.py:177-207):
+ * out[rows of e] = a[rows of e] @ w[e]^T, rows of e = [offsets[e], offsets[e+1]).
+ * a (M, K) bf16/f16, w (E, N, K) same type, out (M, ldo) same type, f32
+ * accumulate on tcgen05 tensor cores. With w_dtype == MOE_DT_I8 this is
+ * grouped_matmul_int8 (src/dispatch/kernels/grouped_gemm_int8.py:141-176): w is
+ * int8, dequantised exactly to the activation type before the MMA, and
+ * scale (E, N) (scale_dtype f32 or bf16) multiplies the accumulator after the
+ * K loop. K must be a multiple of 8 (16 for int8); offsets live on the device.
+ */
+int moe_grouped_gemm(const void* a, int a_dtype, int64_t M, int64_t K, const void* w, int w_dtype,
+                     const void* scale, int scale_dtype, int64_t E, int64_t N, const int32_t* offsets, void* out,
+                     int64_t ldo, int32_t* status, void* stream);
+
+/*
+ * Expert FFN over grouped rows, the three GEMMs plus SwiGLU of
+ * grouped_moe_routed (src/dispatch/kernels/moe_forward.py:65-68) fused into
+ * two tcgen05 launches: h = silu(xs @ gate^T) * (xs @ up^T) with gate and up in
+ * one N=2x128 tile and the activation in the epilogue, then y = h @ down^T.
+ * Routed rows: xs (R, H), offsets (E+1), y (R, H). The optional shared expert
+ * (src/dispatch/kernels/reference_moe.py:50-54,74-78) runs in the same
+ * launches as one more group over all T rows of x_shared: shared_gate/up
+ * (I_s, H), shared_down (H, I_s), y_shared (T, H). Pass NULL shared pointers
+ * and T_shared = 0 to skip it. w_dtype is the routed weights' type (bf16, f16
+ * or int8 with scales); the shared expert is always in the activation type.
+ * workspace: moe_ffn_workspace_bytes (holds h).
+ */
+size_t moe_ffn_workspace_bytes(int64_t R, int64_t I, int64_t T_shared, int64_t I_shared);
+int moe_expert_ffn(const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets, int64_t E,
+                   int64_t I, const void* gate, const void* up, const void* down, int w_dtype,
+                   const void* gate_scale, const void* up_scale, const void* down_scale, int scale_dtype,
+                   const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
+                   const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream);
+/* The same, one half at a time: part 1 = gate/up GEMM + SwiGLU (writes h into
+ * the workspace), part 2 = down GEMM (reads h), part 3 = both. Lets a caller
+ * time or overlap the two launches separately. */
+int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
+                        int64_t E, int64_t I, const void* gate, const void* up, const void* down, int w_dtype,
+                        const void* gate_scale, const void* up_scale, const void* down_scale, int scale_dtype,
+                        const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
+                        const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
+                        size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Weighted combine / unpermute. Replaces ungroup_and_combine
+ * (src/dispatch/kernels/grouping.py:44-61): out[t] = sum_s topk_w[t,s] *
+ * y[pos[t*k+s]] (+ y_shared[t]), summed in slot order in f32 and rounded once
+ * to out_dtype -- deterministic, unlike the reference's index_add_.
+ * y, y_shared in y_dtype (bf16/f16/f32); y_shared may be NULL.
+ */
+int moe_combine(const void* y, int y_dtype, const int32_t* pos, const float* topk_w, int64_t T, int k,
+                int64_t H, const void* y_shared, void* out, int out_dtype, int32_t* status, void* stream);
+
+/*
+ * Per-output-channel int8 quantisation. Replaces quantize_per_channel_int8
+ * (src/dispatch/kernels/quantization.py:31-50): scale = absmax/127 in f32 (1 for
+ * an all-zero channel), q = clamp(round_half_even(w / scale), -127, 127).
+ * w (rows, K) in w_dtype (bf16/f16/f32), q (rows, K) int8, scale (rows) stored
+ * as scale_dtype (f32, or bf16 rounded from the f32 value).
+ */
+int moe_quantize_int8(const void* w, int w_dtype, int64_t rows, int64_t K, int8_t* q, void* scale,
+                      int scale_dtype, void* stream);
+
+/*
+ * Whole layer: route -> group + gather -> expert FFN -> combine, five
+ * launches and no host synchronisation. Replaces ReferenceMoE.forward
+ * (src/dispatch/kernels/reference_moe.py:74-78) and, with topk_in given, the
+ * moe_infer closure of src/dispatch/kernels/integration.py:158-175.
+ * If topk_idx_in/topk_w_in (int32 / f32, (T,k)) are non-NULL the router is
+ * skipped. Outputs: out (T, H) in out_dtype; topk_idx/topk_w (T,k) (written by
+ * the router, or copies of the inputs are not made: pass the same buffers),
+ * counts (E), offsets (E+1) (all may be NULL except out).
+ */
+typedef struct MoeLayerDesc {
+  int64_t T, H, E, I, I_shared;
+  int k;
+  int act_dtype;      /* bf16 or f16: the tensor-core input type */
+  int x_dtype;        /* bf16, f16 or f32 */
+  int out_dtype;      /* bf16, f16 or f32 */
+  int w_dtype;        /* routed weights: act type or MOE_DT_I8 */
+  int scale_dtype;    /* f32 or bf16 (int8 only) */
+  int router_mode;    /* MOE_ROUTER_* */
+  int renorm;
+  int n_group, topk_group;
+  float routed_scaling;
+  int router_w_dtype; /* bf16 or f32 */
+} MoeLayerDesc;
+
+size_t moe_layer_workspace_bytes(const MoeLayerDesc* d);
+int moe_layer_forward(const MoeLayerDesc* d, const void* x, const void* router_w, const float* e_score_bias,
+                      const int32_t* topk_idx_in, const float* topk_w_in, const void* gate, const void* up,
+                      const void* down, const void* gate_scale, const void* up_scale, const void* down_scale,
+                      const void* shared_gate, const void* shared_up, const void* shared_down, void* out,
+                      int32_t* topk_idx, float* topk_w, int32_t* counts, int32_t* offsets, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H_ */
