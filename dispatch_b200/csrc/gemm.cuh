@@ -1,17 +1,18 @@
 // Persistent, warp-specialised grouped GEMM on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA) for the routed expert FFN.
+// (tcgen05 + TMEM + TMA) for the routed expert FFN and the router logits.
 //
-// One launch walks a flat tile space made of up to two "segments" (the routed
-// experts and the shared expert). A segment is a list of row groups (one per
-// expert) over one A matrix, sharing N, K and a stacked (G, N, K) weight. Row
-// offsets of the groups live on the device (written by the grouping kernel), so
-// the tile list is derived in-kernel and the host never synchronises.
+// One launch walks a flat tile space made of up to two "segments" (e.g. the
+// routed experts and the shared expert). A segment is a list of row groups
+// (one per expert) over one A matrix, sharing N, K and a stacked (G, N, K)
+// weight. Row offsets of the groups live on the device (written by the
+// grouping kernel), so the tile list is derived in-kernel and the host never
+// synchronises.
 //
-// Tile = 128 rows x 256 MMA columns, K in blocks of 64 (one 128-byte swizzle
-// atom of bf16). In a SwiGLU segment the 256 columns are 128 gate rows and the
-// 128 matching up rows of the weight, and the epilogue writes
-// h = silu(gate) * up for 128 output columns; in a plain segment all 256
-// columns are outputs.
+// Tile = 128 rows x mma_n MMA columns (mma_n <= 256, per segment), K in blocks
+// of 64 (one 128-byte swizzle atom of bf16). In a SwiGLU segment the mma_n
+// columns are mma_n/2 gate rows and the matching mma_n/2 up rows of the
+// weight, and the epilogue writes h = silu(gate) * up; in a plain segment all
+// mma_n columns are outputs (bf16/f16, or f32 for the router logits).
 //
 // Warp roles (256 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
 // issues tcgen05.mma from one thread, warps 2-3 dequantise int8 weight tiles to
@@ -19,7 +20,7 @@
 // double-buffered TMEM accumulator (lane quarter = warp % 4) and store.
 // Every mbarrier wait is bounded (ptx.cuh); on expiry the CTA drains its
 // in-flight copies and MMAs, frees TMEM and returns with MOE_ERR_TIMEOUT in the
-// status word.
+// status word. Group offsets are validated before use (MOE_ERR_BAD_OFFSETS).
 #pragma once
 #include "ptx.cuh"
 
@@ -28,12 +29,12 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int BN = 256;
+constexpr int BN = 256;  // largest MMA N; TMEM columns per accumulator buffer
 constexpr int kThreads = 256;
 constexpr int kMaxGroups = 256;
 constexpr int kMaxSegs = 2;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
-constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB (largest B stage)
 constexpr uint32_t Q_BYTES = BN * BK;      // 16 KiB int8 staging
 constexpr uint32_t kTmemCols = 2 * BN;     // two accumulators of 256 f32 columns
 constexpr int kConvThreads = 64;           // warps 2-3
@@ -54,19 +55,21 @@ struct Segment {
   void* out;               // (rows, ldo)
   int64_t ldo;
   int groups;
-  int dense_rows;
-  int n;  // output columns
+  int dense_rows;  // rows of A (and of out)
+  int n;           // output columns
   int k;
+  int mma_n;       // MMA N of this segment: multiple of 32 (64 for SwiGLU), <= 256
   int swiglu;
   int b_int8;
   int scale_bf16;
+  int out_f32;
   int pad_;
 };
 
 struct Params {
   Segment seg[kMaxSegs];
   int num_segs;
-  int in_f16;   // A/B element type: 0 bf16, 1 f16 (also the output type)
+  int in_f16;  // A/B element type: 0 bf16, 1 f16 (also the 16-bit output type)
   int32_t* status;
 };
 
@@ -84,21 +87,23 @@ struct Ctrl {
   int mt[kMaxSegs][kMaxGroups + 1];
 };
 
-__host__ __device__ constexpr int out_cols_per_tile(int swiglu) { return swiglu ? BN / 2 : BN; }
+__host__ __device__ __forceinline__ int out_cols_per_tile(const Segment& s) {
+  return s.swiglu ? s.mma_n / 2 : s.mma_n;
+}
 
 struct Tile {
   int seg, group, row0, rows, n_tile;
 };
 
-__device__ __forceinline__ bool decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
+__device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
   int s = 0;
-  while (s < p.num_segs && t >= c.seg_tiles[s]) {
+  while (s + 1 < p.num_segs && t >= c.seg_tiles[s]) {
     t -= c.seg_tiles[s];
     ++s;
   }
-  if (s >= p.num_segs) return false;
   const Segment& S = p.seg[s];
-  const int nt = (S.n + out_cols_per_tile(S.swiglu) - 1) / out_cols_per_tile(S.swiglu);
+  const int oc = out_cols_per_tile(S);
+  const int nt = (S.n + oc - 1) / oc;
   int lo = 0, hi = S.groups;  // largest g in [0, G) with mt[g] * nt <= t
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -112,53 +117,53 @@ __device__ __forceinline__ bool decode_tile(const Ctrl& c, const Params& p, int 
   tl.n_tile = local / mtg;
   tl.row0 = c.off[s][lo] + m_tile * BM;
   tl.rows = min(BM, c.off[s][lo + 1] - tl.row0);
-  return true;
 }
 
 __device__ __forceinline__ float ld_scale(const void* p, int bf16, int64_t i) {
   return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
 }
 
-// Stores 32 consecutive f32 values of one output row as bf16/f16.
-__device__ __forceinline__ void store_row32(void* out, int64_t elem_off, const float (&v)[32], int ncols, int f16,
-                                            bool vec_ok) {
+__device__ __forceinline__ uint32_t pack2(float a, float b, int f16) {
   if (f16) {
-    __half* o = reinterpret_cast<__half*>(out) + elem_off;
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Stores 32 consecutive f32 values of one output row as bf16/f16/f32; only
+// the first ncols are written.
+__device__ __forceinline__ void store_row32(void* out, int64_t elem_off, const float (&v)[32], int ncols, int f16,
+                                            int f32, bool vec_ok) {
+  if (f32) {
+    float* o = reinterpret_cast<float*>(out) + elem_off;
     if (ncols == 32 && vec_ok) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        __half2 h0 = __floats2half2_rn(v[q * 8 + 0], v[q * 8 + 1]);
-        __half2 h1 = __floats2half2_rn(v[q * 8 + 2], v[q * 8 + 3]);
-        __half2 h2 = __floats2half2_rn(v[q * 8 + 4], v[q * 8 + 5]);
-        __half2 h3 = __floats2half2_rn(v[q * 8 + 6], v[q * 8 + 7]);
-        w.x = *reinterpret_cast<uint32_t*>(&h0);
-        w.y = *reinterpret_cast<uint32_t*>(&h1);
-        w.z = *reinterpret_cast<uint32_t*>(&h2);
-        w.w = *reinterpret_cast<uint32_t*>(&h3);
-        reinterpret_cast<uint4*>(o)[q] = w;
-      }
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(o)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     } else {
-      for (int j = 0; j < ncols; ++j) o[j] = __float2half_rn(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) o[j] = v[j];
+    }
+    return;
+  }
+  uint16_t* o = reinterpret_cast<uint16_t*>(out) + elem_off;
+  if (ncols == 32 && vec_ok) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      reinterpret_cast<uint4*>(o)[q] =
+          make_uint4(pack2(v[q * 8 + 0], v[q * 8 + 1], f16), pack2(v[q * 8 + 2], v[q * 8 + 3], f16),
+                     pack2(v[q * 8 + 4], v[q * 8 + 5], f16), pack2(v[q * 8 + 6], v[q * 8 + 7], f16));
     }
   } else {
-    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + elem_off;
-    if (ncols == 32 && vec_ok) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
-        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
-        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
-        w.x = *reinterpret_cast<uint32_t*>(&h0);
-        w.y = *reinterpret_cast<uint32_t*>(&h1);
-        w.z = *reinterpret_cast<uint32_t*>(&h2);
-        w.w = *reinterpret_cast<uint32_t*>(&h3);
-        reinterpret_cast<uint4*>(o)[q] = w;
+    for (int j = 0; j < 32; ++j) {
+      if (j < ncols) {
+        const uint32_t b = pack2(v[j], 0.f, f16);
+        o[j] = static_cast<uint16_t>(b & 0xFFFFu);
       }
-    } else {
-      for (int j = 0; j < ncols; ++j) o[j] = __float2bfloat16_rn(v[j]);
     }
   }
 }
@@ -176,17 +181,8 @@ __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi
       const uint32_t bits = __byte_perm(w[i], 0x4B000000u, 0x7540u | static_cast<uint32_t>(b));
       f[b] = __uint_as_float(bits) - 8388736.0f;
     }
-    if (f16) {
-      __half2 a = __floats2half2_rn(f[0], f[1]);
-      __half2 c = __floats2half2_rn(f[2], f[3]);
-      out[2 * i] = *reinterpret_cast<uint32_t*>(&a);
-      out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&c);
-    } else {
-      __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]);
-      __nv_bfloat162 c = __floats2bfloat162_rn(f[2], f[3]);
-      out[2 * i] = *reinterpret_cast<uint32_t*>(&a);
-      out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&c);
-    }
+    out[2 * i] = pack2(f[0], f[1], f16);
+    out[2 * i + 1] = pack2(f[2], f[3], f16);
   }
   lo = make_uint4(out[0], out[1], out[2], out[3]);
   hi = make_uint4(out[4], out[5], out[6], out[7]);
@@ -259,8 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     }
     bad = __any_sync(0xffffffffu, bad);
     if (lane == 0) {
-      const int nt = (Sg.n + out_cols_per_tile(Sg.swiglu) - 1) / out_cols_per_tile(Sg.swiglu);
-      c.seg_tiles[s] = bad ? 0 : running * nt;
+      const int oc = out_cols_per_tile(Sg);
+      c.seg_tiles[s] = bad ? 0 : running * ((Sg.n + oc - 1) / oc);
       if (bad && p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
     }
   }
@@ -287,31 +283,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
         const int nkb = (Sg.k + BK - 1) / BK;
-        const int n0 = tl.n_tile * out_cols_per_tile(Sg.swiglu);
+        const int n0 = tl.n_tile * out_cols_per_tile(Sg);
+        const bool q8 = kInt8 && Sg.b_int8;
+        const uint32_t row_bytes = q8 ? BK : BK * 2;  // bytes of one weight row in a stage
+        const uint32_t b_bytes = static_cast<uint32_t>(Sg.mma_n) * row_bytes;
+        const uint32_t half = static_cast<uint32_t>(Sg.mma_n / 2) * row_bytes;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
           uint8_t* a_dst = sA + stage * A_BYTES;
-          if (kInt8 && Sg.b_int8) {
-            uint8_t* q_dst = sQ + stage * Q_BYTES;
-            mbar_arrive_expect_tx(&c.full[stage], A_BYTES + Q_BYTES);
-            tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
-            if (Sg.swiglu) {
-              tma_load_3d(q_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
-              tma_load_3d(q_dst + Q_BYTES / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
-            } else {
-              tma_load_3d(q_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
-            }
-          } else {
-            uint8_t* b_dst = sB + stage * B_BYTES;
-            mbar_arrive_expect_tx(&c.full[stage], A_BYTES + B_BYTES);
-            tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
-            if (Sg.swiglu) {
-              tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
-              tma_load_3d(b_dst + B_BYTES / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
-            } else {
-              tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
-            }
-          }
+          uint8_t* b_dst = q8 ? sQ + stage * Q_BYTES : sB + stage * B_BYTES;
+          mbar_arrive_expect_tx(&c.full[stage], A_BYTES + b_bytes);
+          tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
+          tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
+          if (Sg.swiglu) tma_load_3d(b_dst + half, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -331,7 +315,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(BM, BN, p.in_f16 != 0);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       // conv[s] completes a phase only when an int8 tile uses stage s, so its
       // parity is tracked per stage, apart from the full/empty phase.
@@ -342,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
         const int nkb = (Sg.k + BK - 1) / BK;
+        const uint32_t idesc = idesc_f16(BM, Sg.mma_n, p.in_f16 != 0);
         if (!wait_parity_bounded(&c.tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
@@ -392,12 +376,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
         const int nkb = (Sg.k + BK - 1) / BK;
+        const int items = Sg.mma_n * 4;  // 16-byte int8 chunks in one stage
         for (int kb = 0; kb < nkb; ++kb) {
           if (Sg.b_int8) {
             if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) { ok = false; break; }
             const uint8_t* q = sQ + stage * Q_BYTES;
             uint8_t* b = sB + stage * B_BYTES;
-            for (int item = ct; item < BN * 4; item += kConvThreads) {
+            for (int item = ct; item < items; item += kConvThreads) {
               const int r = item >> 2, cc = item & 3;
               const uint4 v = *reinterpret_cast<const uint4*>(q + r * 64 + cc * 16);
               uint4 lo, hi;
@@ -429,13 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
       const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo;
       const bool vec_ok = (Sg.ldo % 8) == 0;
       const int64_t sc_base = static_cast<int64_t>(tl.group) * Sg.n;
+      const int oc = out_cols_per_tile(Sg);
+      const int n0 = tl.n_tile * oc;
       if (Sg.swiglu) {
-        const int n0 = tl.n_tile * (BN / 2);
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < oc / 32; ++ch) {
           uint32_t gv[32], uv[32];
           tmem_ld_32x32b_x32(tb + ch * 32, gv);
-          tmem_ld_32x32b_x32(tb + BN / 2 + ch * 32, uv);
+          tmem_ld_32x32b_x32(tb + oc + ch * 32, uv);
           tmem_ld_wait();
           const int col0 = n0 + ch * 32;
           if (valid && col0 < Sg.n) {
@@ -451,13 +437,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
               }
               h[j] = g / (1.0f + __expf(-g)) * u;
             }
-            store_row32(Sg.out, row_off + col0, h, nc, p.in_f16, vec_ok);
+            store_row32(Sg.out, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
           }
         }
       } else {
-        const int n0 = tl.n_tile * BN;
 #pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < oc / 32; ++ch) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tb + ch * 32, v);
           tmem_ld_wait();
@@ -470,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
               o[j] = __uint_as_float(v[j]);
               if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
             }
-            store_row32(Sg.out, row_off + col0, o, nc, p.in_f16, vec_ok);
+            store_row32(Sg.out, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
           }
         }
       }

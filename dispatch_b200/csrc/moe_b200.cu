@@ -148,13 +148,15 @@ struct SegSpec {
   void* out;
   int64_t ldo;
   bool swiglu;
+  int mma_n = moe::gemm::BN;  // multiple of 32 (64 for SwiGLU), <= 256
+  bool out_f32 = false;
 };
 
 int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   std::memset(s, 0, sizeof(*s));
   int rc = make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
   if (rc) return rc;
-  const int box_rows = sp.swiglu ? moe::gemm::BN / 2 : moe::gemm::BN;
+  const int box_rows = sp.swiglu ? sp.mma_n / 2 : sp.mma_n;
   rc = make_map_b(&s->map_b0, sp.b0, sp.b_dtype, sp.G, sp.N, sp.K, box_rows);
   if (rc) return rc;
   if (sp.swiglu) {
@@ -173,6 +175,8 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   s->swiglu = sp.swiglu ? 1 : 0;
   s->b_int8 = sp.b_dtype == MOE_DT_I8 ? 1 : 0;
   s->scale_bf16 = sp.scale_dtype == MOE_DT_BF16 ? 1 : 0;
+  s->mma_n = sp.mma_n;
+  s->out_f32 = sp.out_f32 ? 1 : 0;
   return MOE_OK;
 }
 
@@ -188,6 +192,9 @@ int check_seg(const SegSpec& sp, int act_dtype) {
             sp.b_dtype, act_dtype);
   const int kmul = sp.b_dtype == MOE_DT_I8 ? 16 : 8;
   CHECK_ARG(sp.K % kmul == 0, "K mismatch: K=%lld must be a multiple of %d", (long long)sp.K, kmul);
+  CHECK_ARG(sp.mma_n >= 32 && sp.mma_n <= moe::gemm::BN && sp.mma_n % (sp.swiglu ? 64 : 32) == 0,
+            "MMA width %d must be a multiple of %d in [32, 256]", sp.mma_n, sp.swiglu ? 64 : 32);
+  CHECK_ARG(!sp.out_f32 || !sp.swiglu, "f32 output is for plain segments");
   CHECK_ARG(sp.lda % 8 == 0 && aligned16(sp.a) && aligned16(sp.b0) && (!sp.b1 || aligned16(sp.b1)),
             "operands must be 16-byte aligned with row strides a multiple of 16 bytes");
   if (sp.b_dtype == MOE_DT_I8) {
@@ -226,7 +233,7 @@ int run_gemm(const SegSpec* specs, int nseg, int act_dtype, int32_t* status, cud
     rc = fill_segment(&p.seg[i], specs[i], act_dtype);
     if (rc) return rc;
     any_i8 |= specs[i].b_dtype == MOE_DT_I8;
-    const int oc = moe::gemm::out_cols_per_tile(specs[i].swiglu);
+    const int oc = specs[i].swiglu ? specs[i].mma_n / 2 : specs[i].mma_n;
     const int64_t mt = (specs[i].a_rows + moe::gemm::BM - 1) / moe::gemm::BM + (specs[i].offsets ? specs[i].G : 0);
     tiles_bound += mt * ((specs[i].N + oc - 1) / oc);
   }
@@ -286,6 +293,7 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   if (!logits_in) {
     CHECK_ARG(x_dtype == MOE_DT_BF16 || x_dtype == MOE_DT_F16 || x_dtype == MOE_DT_F32, "bad x dtype");
     CHECK_ARG(w_dtype == MOE_DT_BF16 || w_dtype == MOE_DT_F16 || w_dtype == MOE_DT_F32, "bad router dtype");
+    CHECK_ARG(H % 8 == 0 && aligned16(x) && aligned16(router_w), "H must be a multiple of 8, x/router_w aligned");
   }
   CHECK_ARG(mode == MOE_ROUTER_SOFTMAX || mode == MOE_ROUTER_SIGMOID_GROUP, "unknown router mode %d", mode);
   if (mode == MOE_ROUTER_SIGMOID_GROUP) {
@@ -294,6 +302,33 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
     CHECK_ARG(static_cast<int64_t>(topk_group) * (E / n_group) >= k, "kept groups hold fewer than top_k experts");
   }
   if (T == 0) return MOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // bf16/f16 x and router weight: the logits are a dense tcgen05 GEMM with an
+  // f32 epilogue (into logits_out), then the selection kernel reads them.
+  const bool tensor_logits = !logits_in && is16(x_dtype) && w_dtype == x_dtype && H % 8 == 0 && aligned16(x) &&
+                             aligned16(router_w);
+  if (tensor_logits) {
+    CHECK_ARG(logits_out, "logits_out (T, E) f32 is required when the logits are computed from bf16/f16 x");
+    SegSpec sp{};
+    sp.a = x;
+    sp.a_rows = T;
+    sp.lda = H;
+    sp.b0 = router_w;
+    sp.b_dtype = w_dtype;
+    sp.G = 1;
+    sp.N = E;
+    sp.K = H;
+    sp.offsets = nullptr;
+    sp.out = logits_out;
+    sp.ldo = E;
+    sp.swiglu = false;
+    sp.mma_n = static_cast<int>((E + 31) / 32 * 32);
+    sp.out_f32 = true;
+    rc = run_gemm(&sp, 1, x_dtype, status, s);
+    if (rc) return rc;
+    logits_in = logits_out;
+    logits_out = nullptr;
+  }
   moe::route::Params p;
   p.x = x;
   p.w = router_w;
@@ -321,8 +356,7 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
     cudaFuncSetAttribute(moe::route::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
   });
   const int64_t grid = (T + p.tb - 1) / p.tb;
-  moe::route::route_kernel<<<static_cast<unsigned>(grid), moe::route::kThreads, smem,
-                             static_cast<cudaStream_t>(stream)>>>(p);
+  moe::route::route_kernel<<<static_cast<unsigned>(grid), moe::route::kThreads, smem, s>>>(p);
   CUDA_TRY(cudaGetLastError(), "route_kernel launch");
   return MOE_OK;
 }
@@ -535,7 +569,7 @@ int moe_quantize_int8(const void* w, int w_dtype, int64_t rows, int64_t K, int8_
 // ------------------------------------------------------------------ layer
 namespace {
 struct LayerWs {
-  size_t idx, w, counts, offsets, pos, xs, y, ys, group, ffn, total;
+  size_t idx, w, logits, counts, offsets, pos, xs, y, ys, group, ffn, total;
 };
 LayerWs layer_ws(const MoeLayerDesc* d) {
   auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
@@ -544,6 +578,7 @@ LayerWs layer_ws(const MoeLayerDesc* d) {
   const bool shared = d->I_shared > 0;
   size_t o = 0;
   l.idx = o; o += up(R * 4);
+  l.logits = o; o += up(T * static_cast<size_t>(d->E) * 4);
   l.w = o; o += up(R * 4);
   l.counts = o; o += up(static_cast<size_t>(d->E) * 4);
   l.offsets = o; o += up(static_cast<size_t>(d->E + 1) * 4);
@@ -588,7 +623,8 @@ int moe_layer_forward(const MoeLayerDesc* d, const void* x, const void* router_w
     wts = const_cast<float*>(topk_w_in);
   } else {
     rc = moe_route(x, d->x_dtype, router_w, d->router_w_dtype, nullptr, d->T, d->H, d->E, d->k, d->router_mode,
-                   d->renorm, e_score_bias, d->n_group, d->topk_group, d->routed_scaling, idx, wts, nullptr, status,
+                   d->renorm, e_score_bias, d->n_group, d->topk_group, d->routed_scaling, idx, wts,
+                   reinterpret_cast<float*>(ws + l.logits), status,
                    stream);
     if (rc) return rc;
   }

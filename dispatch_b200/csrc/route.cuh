@@ -39,6 +39,31 @@ __device__ __forceinline__ float to_f32(const void* p, int dt, int64_t i) {
   return reinterpret_cast<const float*>(p)[i];
 }
 
+// 8 consecutive elements as f32 (16-byte aligned): one 16-byte load for 16-bit
+// types, two for f32.
+__device__ __forceinline__ void load8f(const void* p, int dt, int64_t i, float (&v)[8]) {
+  if (dt == MOE_DT_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    return;
+  }
+  const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (dt == MOE_DT_BF16) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+      v[2 * j] = __low2float(h);
+      v[2 * j + 1] = __high2float(h);
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
+      v[2 * j] = __low2float(h);
+      v[2 * j + 1] = __high2float(h);
+    }
+  }
+}
+
 // Warp arg-max: larger value wins, equal values go to the lower index.
 __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 #pragma unroll
@@ -70,8 +95,9 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
   const int E = p.E;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tb;
   const int ntok = static_cast<int>((p.T - t0) < tb ? (p.T - t0) : tb);
-  float* lg = smem_f;                 // [tb][E] logits
-  float* xs = smem_f + tb * E;        // [tb][H] x rows (compute mode)
+  // [tb][H] x rows (compute mode; 16-byte aligned since H % 8 == 0), then [tb][E] logits
+  float* xs = smem_f;
+  float* lg = smem_f + (p.logits_in ? 0 : static_cast<int64_t>(tb) * p.H);
   __shared__ float cbuf[kWarps][kMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -86,11 +112,22 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
       float acc[kMaxTB];
 #pragma unroll
       for (int t = 0; t < kMaxTB; ++t) acc[t] = 0.f;
-      for (int64_t h = lane; h < H; h += 32) {
-        const float wv = to_f32(p.w, p.w_dtype, static_cast<int64_t>(e) * H + h);
+      // 8 consecutive weights per lane per step (H % 8 == 0, checked on the host)
+#pragma unroll 2
+      for (int64_t h = lane * 8; h < H; h += 256) {
+        float wv[8];
+        load8f(p.w, p.w_dtype, static_cast<int64_t>(e) * H + h, wv);
 #pragma unroll
-        for (int t = 0; t < kMaxTB; ++t)
-          if (t < ntok) acc[t] = fmaf(xs[t * H + h], wv, acc[t]);
+        for (int t = 0; t < kMaxTB; ++t) {
+          if (t < ntok) {
+            const float4 a = *reinterpret_cast<const float4*>(xs + t * H + h);
+            const float4 b = *reinterpret_cast<const float4*>(xs + t * H + h + 4);
+            float s = acc[t];
+            s = fmaf(a.x, wv[0], s); s = fmaf(a.y, wv[1], s); s = fmaf(a.z, wv[2], s); s = fmaf(a.w, wv[3], s);
+            s = fmaf(b.x, wv[4], s); s = fmaf(b.y, wv[5], s); s = fmaf(b.z, wv[6], s); s = fmaf(b.w, wv[7], s);
+            acc[t] = s;
+          }
+        }
       }
 #pragma unroll
       for (int t = 0; t < kMaxTB; ++t) {
@@ -102,13 +139,15 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
     }
   }
   __syncthreads();
+  // logits_out holds the raw gate output, before any bias
+  if (p.logits_out)
+    for (int i = threadIdx.x; i < ntok * E; i += kThreads) p.logits_out[t0 * E + i] = lg[i];
   if (p.mode == MOE_ROUTER_SOFTMAX && p.bias) {
     // softmax mode: the bias is part of the logits (a gate Linear with bias)
+    __syncthreads();
     for (int i = threadIdx.x; i < ntok * E; i += kThreads) lg[i] += p.bias[i % E];
     __syncthreads();
   }
-  if (p.logits_out)
-    for (int i = threadIdx.x; i < ntok * E; i += kThreads) p.logits_out[t0 * E + i] = lg[i];
 
   constexpr int J = kMaxE / 32;
   for (int t = warp; t < ntok; t += kWarps) {

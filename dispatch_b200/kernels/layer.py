@@ -118,7 +118,9 @@ def route(
 ):
     """Router only: (topk_idx int32 (T,k), topk_weight f32 (T,k)[, logits f32]).
     With ``logits`` given the selection runs on exactly those values (the
-    parity boundary "same logits in -> same ids out")."""
+    parity boundary "same logits in -> same ids out"). Returned logits are the
+    raw gate output x @ router_weight.T; in softmax mode ``e_score_bias`` is
+    added to them before the selection."""
     ref = logits if logits is not None else x
     dev = L.require_cuda(ref, router_weight if logits is None else None, e_score_bias, what="route")
     if logits is not None:
@@ -133,7 +135,8 @@ def route(
     k = router.top_k
     idx = torch.empty(t, k, dtype=torch.int32, device=dev)
     w = torch.empty(t, k, dtype=torch.float32, device=dev)
-    lg = torch.empty(t, e, dtype=torch.float32, device=dev) if return_logits else None
+    # the tensor-core logit GEMM writes here (needed whenever x is given)
+    lg = torch.empty(t, e, dtype=torch.float32, device=dev) if (return_logits or logits is None) else None
     bias = None if e_score_bias is None else e_score_bias.contiguous().float()
     rc = L.lib().moe_route(
         None if logits is not None else x.data_ptr(), 0 if logits is not None else L.dt(x),

@@ -74,7 +74,10 @@ int moe_device_sm_count(void);
  * MOE_ROUTER_SIGMOID_GROUP the group-limited sigmoid selection with
  * e_score_bias (E floats, may be NULL), n_group / topk_group, renorm and
  * routed_scaling. When logits_in is non-NULL it is used instead of x/router_w
- * (x and router_w may then be NULL). logits_out (T, E) f32 may be NULL.
+ * (x and router_w may then be NULL). With bf16/f16 x and a router weight of the
+ * same type the logits are a dense tcgen05 GEMM written to logits_out (T, E)
+ * f32, which is then required; otherwise (f32 inputs) a CUDA-core kernel
+ * computes them and logits_out may be NULL. H must be a multiple of 8.
  */
 int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, const float* logits_in, int64_t T,
               int64_t H, int64_t E, int k, int mode, int renorm, const float* e_score_bias, int n_group,

@@ -240,7 +240,9 @@ def test_layer_c2_bf16_with_shared_experts(c2_weights: LayerWeights, t: int, ske
     res = moe_layer_forward(x, lw.router, StackedExpertWeights(lw.gate, lw.up, lw.down), RouterConfig(top_k=6),
                             shared=SharedExpertWeights(*lw.shared), e_score_bias=bias)
     _, _, lg = route(x, lw.router, RouterConfig(top_k=6), e_score_bias=bias, return_logits=True)
-    ids, w = O.route_softmax_topk(lg.cpu().numpy(), 6)
+    # returned logits are the raw gate output; the bias is added before selection
+    biased = lg.cpu().numpy() + (O.zipf_bias(64) if skew else 0.0)
+    ids, w = O.route_softmax_topk(biased, 6)
     np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), ids)
     np.testing.assert_allclose(res.topk_weight.cpu().numpy(), w, rtol=2e-6, atol=1e-7)
     np.testing.assert_array_equal(res.group_sizes.cpu().numpy(), np.bincount(ids.reshape(-1), minlength=64))
