@@ -67,6 +67,10 @@ _SIGNATURES = {
         [_p, _i32, _p, _i64, _i32, _i64, _p, _p, _p, _p, _p, _p, _i32, _i64, _p, _i32, _p, _sz, _p, _p],
         _i32,
     ),
+    "moe_group_tokens_noalloc": (
+        [_p, _i32, _p, _i64, _i32, _i64, _p, _p, _p, _p, _p, _p, _i32, _i64, _p, _i32, _p, _p],
+        _i32,
+    ),
     "moe_grouped_gemm": ([_p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i64, _i64, _p, _p, _i64, _p, _p], _i32),
     "moe_ffn_workspace_bytes": ([_i64, _i64, _i64, _i64], _sz),
     "moe_expert_ffn": (

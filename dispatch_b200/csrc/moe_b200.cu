@@ -420,6 +420,105 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
   return MOE_OK;
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation grouping
+// Scratch of moe_group_tokens_noalloc: the per-chunk expert histograms live in
+// this fixed array of the library's device image instead of a caller buffer.
+// Every device that loads the library holds these 1 MiB until the process exits.
+static __device__ __align__(256) int32_t g_group_scratch[MOE_GROUP_NOALLOC_SCRATCH_INTS];
+
+namespace {
+struct ScratchSlot {
+  std::once_flag once;
+  int32_t* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+std::array<ScratchSlot, kMaxDevices> g_scratch;
+
+// Device address of g_group_scratch on the current device. On the host the
+// symbol name is only a stand-in, so the address is looked up once per
+// device, with that device current, on the first call.
+int group_scratch(int32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(MOE_ERR_NO_DEVICE, "no CUDA device is current");
+  ScratchSlot& slot = g_scratch[dev];
+  std::call_once(slot.once, [&] {
+    void* p = nullptr;
+    slot.err = cudaGetSymbolAddress(&p, g_group_scratch);
+    slot.ptr = static_cast<int32_t*>(p);
+  });
+  if (slot.err != cudaSuccess || slot.ptr == nullptr) return cuda_fail(slot.err, "cudaGetSymbolAddress(group scratch)");
+  *out = slot.ptr;
+  return MOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int moe_group_tokens_noalloc(const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T, int k, int64_t E,
+                             int32_t* counts, int32_t* offsets, int32_t* pos, int64_t* sorted_token_idx,
+                             float* sorted_weight, const void* x, int x_dtype, int64_t H, void* xs, int xs_dtype,
+                             int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(E >= 1 && E <= moe::group::kMaxE, "E=%lld must be in [1, %d]", (long long)E, moe::group::kMaxE);
+  CHECK_ARG(k >= 1 && T >= 0, "bad T/k");
+  const int64_t n = T * k;
+  const int64_t chunks = (n + moe::group::kChunk - 1) / moe::group::kChunk;
+  CHECK_ARG(chunks * E <= MOE_GROUP_NOALLOC_SCRATCH_INTS,
+            "moe_group_tokens_noalloc: ceil(T*k/256)*E = %lld exceeds the built-in scratch of %d int32 "
+            "(T*k=%lld, E=%lld); use moe_group_tokens with a caller workspace",
+            (long long)(chunks * E), MOE_GROUP_NOALLOC_SCRATCH_INTS, (long long)n, (long long)E);
+  CHECK_ARG(idx_dtype == MOE_DT_I32 || idx_dtype == MOE_DT_I64, "topk_idx must be int32 or int64");
+  CHECK_ARG(counts && offsets && pos, "null output pointer");
+  CHECK_ARG(!sorted_weight || topk_w, "sorted_weight needs topk_w");
+  if (xs) {
+    CHECK_ARG(x && H >= 8 && H % 8 == 0, "gather needs x and H a multiple of 8");
+    CHECK_ARG(is16(xs_dtype), "xs dtype must be bf16 or f16");
+    CHECK_ARG(x_dtype == MOE_DT_F32 || x_dtype == xs_dtype, "x dtype must be f32 or match xs");
+    CHECK_ARG(aligned16(x) && aligned16(xs), "x/xs must be 16-byte aligned");
+  }
+  int32_t* scratch = nullptr;
+  rc = group_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    CUDA_TRY(cudaMemsetAsync(counts, 0, E * sizeof(int32_t), s), "memset counts");
+    CUDA_TRY(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), s), "memset offsets");
+    return MOE_OK;
+  }
+  moe::group::Params p;
+  p.idx = topk_idx;
+  p.idx64 = idx_dtype == MOE_DT_I64;
+  p.w = topk_w;
+  p.n = n;
+  p.k = k;
+  p.E = static_cast<int>(E);
+  p.nchunks = static_cast<int>(chunks);
+  p.counts = counts;
+  p.offsets = offsets;
+  p.pos = pos;
+  p.sorted_token_idx = sorted_token_idx;
+  p.sorted_weight = sorted_weight;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.H = H;
+  p.xs = xs;
+  p.xs_f16 = xs_dtype == MOE_DT_F16;
+  // The histogram kernel writes every scratch entry the scatter kernel reads,
+  // so the scratch needs no clearing between calls.
+  p.hist = scratch;
+  p.status = status;
+  moe::group::group_hist_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
+  CUDA_TRY(cudaGetLastError(), "group_hist_kernel launch");
+  moe::group::group_scatter_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
+  CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
+  return MOE_OK;
+}
+
 int moe_grouped_gemm(const void* a, int a_dtype, int64_t M, int64_t K, const void* w, int w_dtype,
                      const void* scale, int scale_dtype, int64_t E, int64_t N, const int32_t* offsets, void* out,
                      int64_t ldo, int32_t* status, void* stream) {

@@ -104,6 +104,29 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
                      void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * Token grouping without a workspace argument. It has no counterpart in the
+ * reference: it exists for callers that cannot allocate device memory, such
+ * as a host runtime that binds this library over FFI and can only hand over
+ * buffers it already owns, or code running where a cudaMalloc would stall the
+ * device or is forbidden by a fixed memory plan. Same arguments, outputs and
+ * kernels as moe_group_tokens; the per-chunk histograms go to a fixed array
+ * compiled into the library (MOE_GROUP_NOALLOC_SCRATCH_INTS int32 = 1 MiB,
+ * resident on every device that loads the library until the process exits).
+ * Limit: ceil(T*k/256) * E <= MOE_GROUP_NOALLOC_SCRATCH_INTS (e.g. T*k up to
+ * 262144 pairs with E = 256), else MOE_ERR_INVALID_ARG and nothing runs.
+ * The first call on each device looks up the array's device address with that
+ * device current; make that first call before any stream capture. All calls
+ * on a device share the one array (nothing in it needs to start at zero), so
+ * calls that overlap on the GPU -- concurrent streams, or host threads sharing
+ * a device -- race and must be serialised by the caller.
+ */
+#define MOE_GROUP_NOALLOC_SCRATCH_INTS (256 * 1024)
+int moe_group_tokens_noalloc(const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T, int k, int64_t E,
+                             int32_t* counts, int32_t* offsets, int32_t* pos, int64_t* sorted_token_idx,
+                             float* sorted_weight, const void* x, int x_dtype, int64_t H, void* xs, int xs_dtype,
+                             int32_t* status, void* stream);
+
+/*
  * Grouped GEMM, the GroupedMatmul contract (src/dispatch/kernels/moe_forward.py:21,
  * grouped_matmul at src/dispatch/kernels/grouped_gemm.py:177-207):
  * out[rows of e] = a[rows of e] @ w[e]^T, rows of e = [offsets[e], offsets[e+1]).
