@@ -112,6 +112,8 @@ def dist_setup(n: int):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # plain NCCL all-to-all; NVLS multicast is neither needed nor wanted
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     if world != n:
         raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
@@ -276,7 +278,7 @@ def run_b200(args) -> None:
         parallelism = f"ep{world}"
     else:
         step = lambda: moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)  # noqa: E731
-        launches_per_step = 6  # route, group x2, gate/up GEMM, down GEMM, combine
+        launches_per_step = 7  # router GEMM + select, group x2, gate/up GEMM, down GEMM, combine
         parallelism = "single"
 
     res = moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)

@@ -83,6 +83,11 @@ _SIGNATURES = {
          _p, _p, _p, _p, _sz, _p, _p],
         _i32,
     ),
+    "moe_expert_ffn_grouped": (
+        [_i32, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _p,
+         _p, _p, _p, _p, _p, _sz, _p, _p],
+        _i32,
+    ),
     "moe_combine": ([_p, _i32, _p, _p, _i64, _i32, _i64, _p, _p, _i32, _p, _p], _i32),
     "moe_quantize_int8": ([_p, _i32, _i64, _i64, _p, _p, _i32, _p], _i32),
     "moe_layer_workspace_bytes": ([ctypes.POINTER(MoeLayerDesc)], _sz),

@@ -63,7 +63,7 @@ struct Segment {
   int b_int8;
   int scale_bf16;
   int out_f32;
-  int pad_;
+  int weight_mod;  // group g multiplies weight g % weight_mod (expert-parallel: (rank, expert) groups)
 };
 
 struct Params {
@@ -92,7 +92,7 @@ __host__ __device__ __forceinline__ int out_cols_per_tile(const Segment& s) {
 }
 
 struct Tile {
-  int seg, group, row0, rows, n_tile;
+  int seg, group, widx, row0, rows, n_tile;
 };
 
 __device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
@@ -114,6 +114,7 @@ __device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int 
   const int m_tile = local % mtg;
   tl.seg = s;
   tl.group = lo;
+  tl.widx = lo % S.weight_mod;
   tl.n_tile = local / mtg;
   tl.row0 = c.off[s][lo] + m_tile * BM;
   tl.rows = min(BM, c.off[s][lo + 1] - tl.row0);
@@ -294,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
           uint8_t* b_dst = q8 ? sQ + stage * Q_BYTES : sB + stage * B_BYTES;
           mbar_arrive_expect_tx(&c.full[stage], A_BYTES + b_bytes);
           tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
-          tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.group);
-          if (Sg.swiglu) tma_load_3d(b_dst + half, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.group);
+          tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
+          if (Sg.swiglu) tma_load_3d(b_dst + half, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
       const bool valid = r < tl.rows;
       const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo;
       const bool vec_ok = (Sg.ldo % 8) == 0;
-      const int64_t sc_base = static_cast<int64_t>(tl.group) * Sg.n;
+      const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
       const int oc = out_cols_per_tile(Sg);
       const int n0 = tl.n_tile * oc;
       if (Sg.swiglu) {

@@ -143,7 +143,8 @@ struct SegSpec {
   const void* scale0;
   const void* scale1;
   int scale_dtype;
-  int64_t G, N, K;
+  int64_t G, N, K;         // G row groups (offsets has G+1 entries)
+  int64_t Gw = 0;          // weight experts; group g uses weight g % Gw (0 => Gw = G)
   const int32_t* offsets;  // nullptr => dense over a_rows
   void* out;
   int64_t ldo;
@@ -157,10 +158,11 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   int rc = make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
   if (rc) return rc;
   const int box_rows = sp.swiglu ? sp.mma_n / 2 : sp.mma_n;
-  rc = make_map_b(&s->map_b0, sp.b0, sp.b_dtype, sp.G, sp.N, sp.K, box_rows);
+  const int64_t gw = sp.Gw > 0 ? sp.Gw : sp.G;
+  rc = make_map_b(&s->map_b0, sp.b0, sp.b_dtype, gw, sp.N, sp.K, box_rows);
   if (rc) return rc;
   if (sp.swiglu) {
-    rc = make_map_b(&s->map_b1, sp.b1, sp.b_dtype, sp.G, sp.N, sp.K, box_rows);
+    rc = make_map_b(&s->map_b1, sp.b1, sp.b_dtype, gw, sp.N, sp.K, box_rows);
     if (rc) return rc;
   }
   s->offsets = sp.offsets;
@@ -169,6 +171,7 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   s->out = sp.out;
   s->ldo = sp.ldo;
   s->groups = static_cast<int>(sp.offsets ? sp.G : 1);
+  s->weight_mod = static_cast<int>(sp.offsets ? gw : 1);
   s->dense_rows = static_cast<int>(sp.a_rows);
   s->n = static_cast<int>(sp.N);
   s->k = static_cast<int>(sp.K);
@@ -554,7 +557,20 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                         const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
                         const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
                         size_t workspace_bytes, int32_t* status, void* stream) {
+  return moe_expert_ffn_grouped(part, xs, act_dtype, R, H, offsets, E, E, I, gate, up, down, w_dtype, gate_scale,
+                                up_scale, down_scale, scale_dtype, x_shared, T_shared, I_shared, shared_gate,
+                                shared_up, shared_down, y, y_shared, workspace, workspace_bytes, status, stream);
+}
+
+int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
+                           int64_t G, int64_t E, int64_t I, const void* gate, const void* up, const void* down,
+                           int w_dtype, const void* gate_scale, const void* up_scale, const void* down_scale,
+                           int scale_dtype, const void* x_shared, int64_t T_shared, int64_t I_shared,
+                           const void* shared_gate, const void* shared_up, const void* shared_down, void* y,
+                           void* y_shared, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
   CHECK_ARG(part >= 1 && part <= 3, "part must be 1 (gate/up), 2 (down) or 3 (both)");
+  CHECK_ARG(E >= 1 && G >= E && G % E == 0, "groups G=%lld must be a positive multiple of the experts E=%lld",
+            (long long)G, (long long)E);
   const bool has_shared = T_shared > 0 && x_shared;
   CHECK_ARG(workspace && workspace_bytes >= moe_ffn_workspace_bytes(R, I, has_shared ? T_shared : 0, I_shared),
             "workspace too small");
@@ -570,11 +586,11 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
   if (R > 0) {
     SegSpec a{};
     a.a = xs; a.a_rows = R; a.lda = H; a.b0 = gate; a.b1 = up; a.b_dtype = w_dtype; a.scale0 = gate_scale;
-    a.scale1 = up_scale; a.scale_dtype = scale_dtype; a.G = E; a.N = I; a.K = H; a.offsets = offsets; a.out = h;
-    a.ldo = I; a.swiglu = true;
+    a.scale1 = up_scale; a.scale_dtype = scale_dtype; a.G = G; a.Gw = E; a.N = I; a.K = H; a.offsets = offsets;
+    a.out = h; a.ldo = I; a.swiglu = true;
     SegSpec b{};
     b.a = h; b.a_rows = R; b.lda = I; b.b0 = down; b.b_dtype = w_dtype; b.scale0 = down_scale;
-    b.scale_dtype = scale_dtype; b.G = E; b.N = H; b.K = I; b.offsets = offsets; b.out = y; b.ldo = H;
+    b.scale_dtype = scale_dtype; b.G = G; b.Gw = E; b.N = H; b.K = I; b.offsets = offsets; b.out = y; b.ldo = H;
     b.swiglu = false;
     g1[n] = a;
     g2[n] = b;

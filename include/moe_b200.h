@@ -172,6 +172,21 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                         size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * The expert FFN over G = R * E row groups for expert parallelism: group g
+ * (offsets has G+1 entries) is multiplied by weight g % E, so rows received
+ * from R source ranks in (source rank, local expert) order are processed where
+ * they landed, with no regrouping copy. Replaces the local compute of
+ * make_ep_moe_infer (src/dispatch/kernels/expert_parallel.py:170-178). Other
+ * arguments as moe_expert_ffn_part; with G == E it is moe_expert_ffn_part.
+ */
+int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
+                           int64_t G, int64_t E, int64_t I, const void* gate, const void* up, const void* down,
+                           int w_dtype, const void* gate_scale, const void* up_scale, const void* down_scale,
+                           int scale_dtype, const void* x_shared, int64_t T_shared, int64_t I_shared,
+                           const void* shared_gate, const void* shared_up, const void* shared_down, void* y,
+                           void* y_shared, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
  * Weighted combine / unpermute. Replaces ungroup_and_combine
  * (src/dispatch/kernels/grouping.py:44-61): out[t] = sum_s topk_w[t,s] *
  * y[pos[t*k+s]] (+ y_shared[t]), summed in slot order in f32 and rounded once

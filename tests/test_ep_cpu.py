@@ -1,0 +1,165 @@
+"""The expert-parallel exchange on CPU: two gloo ranks run EPLayer with the
+oracle standing in for the kernels (the orchestration under test is the
+count exchange, split sizes, (source, expert) grouping and the two row
+all-to-alls). The result must equal the single-process oracle forward over all
+ranks' tokens. A second test makes one rank fail between its collectives and
+checks that the other rank's next collective ends with an error instead of
+waiting forever."""
+
+from __future__ import annotations
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dispatch_b200.kernels.expert_parallel import EPLayer, Grouped, assign_experts_to_ranks, exchange_layout
+from oracle import moe_oracle as O
+
+H, I, E, K, I_SH, T = 16, 24, 8, 3, 32, 13
+
+
+def _weights():
+    rng = np.random.default_rng(0)
+    f = lambda *s: (rng.standard_normal(s) / np.sqrt(s[-1])).astype(np.float32)  # noqa: E731
+    return f(E, H), f(E, I, H), f(E, I, H), f(E, H, I), (f(I_SH, H), f(I_SH, H), f(H, I_SH))
+
+
+def _tokens(rank: int):
+    return np.random.default_rng(100 + rank).standard_normal((T + rank, H)).astype(np.float32)
+
+
+class OracleOps:
+    """Compute steps of the layer restated with the CPU oracle."""
+
+    def __init__(self, rank: int, world: int):
+        self.router, gate, up, down, self.shared = _weights()
+        e_loc = E // world
+        sl = slice(rank * e_loc, (rank + 1) * e_loc)
+        self.gate, self.up, self.down = gate[sl], up[sl], down[sl]
+        self.e_loc = e_loc
+
+    def route_and_group(self, x: torch.Tensor, n_experts: int) -> Grouped:
+        xn = x.numpy()
+        ids, w = O.route_softmax_topk(xn @ self.router.T, K)
+        g = O.group_tokens_by_expert(ids, w, n_experts)
+        offs = O.group_offsets(g.group_sizes)
+        return Grouped(torch.from_numpy(g.group_sizes.astype(np.int32)), torch.from_numpy(offs.astype(np.int32)),
+                       torch.from_numpy(g.pos.astype(np.int32)), torch.from_numpy(xn[g.sorted_token_idx]),
+                       torch.from_numpy(w))
+
+    def ffn(self, recv_x, recv_offsets, n_groups, x):
+        xr = recv_x.numpy()
+        off = recv_offsets.tolist()
+        y = np.zeros((xr.shape[0], H), np.float32)
+        for g in range(n_groups):
+            s, t = off[g], off[g + 1]
+            if t > s:
+                e = g % self.e_loc
+                y[s:t] = O.swiglu_mlp(xr[s:t], self.gate[e], self.up[e], self.down[e])
+        ys = O.swiglu_mlp(x.numpy(), *self.shared)
+        return torch.from_numpy(y), torch.from_numpy(ys)
+
+    def combine(self, y_back, gr: Grouped, t, k, ys, out_dtype):
+        y = y_back.numpy()
+        pos = gr.pos.numpy()
+        w = gr.topk_weight.numpy().reshape(-1)
+        out = np.zeros((t, H), np.float32)
+        for s in range(k):
+            f = np.arange(t) * k + s
+            out += y[pos[f]] * w[f][:, None]
+        return torch.from_numpy(out + ys.numpy())
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank: int, world: int, port: int, timeout_s: float = 60.0) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=timeout_s))
+
+
+def _ep_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    _init(rank, world, port)
+    try:
+        from dispatch_b200.kernels.layer import RouterConfig
+
+        layer = EPLayer(None, None, None, RouterConfig(top_k=K), rank=rank, world=world, n_experts=E,
+                        ops=OracleOps(rank, world))
+        out = layer(torch.from_numpy(_tokens(rank)))
+        np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_ep_exchange_matches_single_process_forward(world: int, tmp_path) -> None:
+    mp.spawn(_ep_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    router, gate, up, down, shared = _weights()
+    xs = [_tokens(r) for r in range(world)]
+    ref, _, _ = O.moe_forward(np.concatenate(xs), router, gate, up, down, K, shared=shared)
+    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(world)])
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def _failing_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    _init(rank, world, port, timeout_s=5.0)
+    counts = torch.tensor([3, 1, 0, 2], dtype=torch.int32)
+    try:
+        if rank == 1:
+            raise RuntimeError("rank 1 fails before its exchange")  # leaves between collectives
+        try:
+            exchange_layout(counts, world)
+            status = "completed"
+        except RuntimeError as exc:  # the peer never joins: the collective ends with an error
+            status = f"error: {type(exc).__name__}"
+        with open(os.path.join(out_dir, "status0.txt"), "w") as f:
+            f.write(status)
+    except RuntimeError:
+        pass
+
+
+def test_a_rank_that_leaves_makes_the_peer_collective_fail_not_hang(tmp_path) -> None:
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank did not finish: the failed exchange hung")
+    status = (tmp_path / "status0.txt").read_text()
+    assert status.startswith("error"), status
+
+
+def test_exchange_layout_single_rank_is_identity() -> None:
+    port = _free_port()
+    _init(0, 1, port)
+    try:
+        counts = torch.tensor([2, 0, 5, 1], dtype=torch.int32)
+        layout, recv = exchange_layout(counts, 1)
+        assert layout.send_splits == [8] and layout.recv_splits == [8]
+        assert layout.recv_offsets == [0, 2, 2, 7, 8]
+        assert torch.equal(recv, counts)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_assign_experts_to_ranks_mirror() -> None:
+    r = assign_experts_to_ranks(64, 2)
+    assert r[:32].eq(0).all() and r[32:].eq(1).all()
+    with pytest.raises(ValueError, match="fewer than"):
+        assign_experts_to_ranks(1, 2)
+    with pytest.raises(ValueError, match="positive"):
+        assign_experts_to_ranks(0, 2)
