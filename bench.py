@@ -362,6 +362,7 @@ def gateup_roofline(x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
     from dispatch_b200.kernels.grouping import _group
 
     t = x.shape[0]
+    # the layer's own configuration: routed rows pre-gathered by the grouping kernel
     _, offsets, _, _, _, _, xs = _group(res.topk_idx, res.topk_weight, E, x=x, xs_dtype=torch.bfloat16,
                                          want_sorted=False)
     r = xs.shape[0]
@@ -372,12 +373,12 @@ def gateup_roofline(x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
     ys = torch.empty(t, H, dtype=torch.bfloat16, device=dev)
 
     def part(p):
-        rc = lib.moe_expert_ffn_part(
-            p, xs.data_ptr(), L.DT_BF16, r, H, offsets.data_ptr(), E, I, ws.gate.data_ptr(), ws.up.data_ptr(),
-            ws.down.data_ptr(), L.DT_BF16, None, None, None, 0, x.data_ptr(), t, I_SHARED, sh.gate.data_ptr(),
-            sh.up.data_ptr(), sh.down.data_ptr(), y.data_ptr(), ys.data_ptr(), wsb.data_ptr(), nbytes,
-            L.status_word(dev).data_ptr(), stream.cuda_stream)
-        L.check(rc, "moe_expert_ffn_part")
+        rc = lib.moe_expert_ffn_grouped(
+            p, xs.data_ptr(), L.DT_BF16, r, H, offsets.data_ptr(), E, E, None, 0, I, ws.gate.data_ptr(),
+            ws.up.data_ptr(), ws.down.data_ptr(), L.DT_BF16, None, None, None, 0, x.data_ptr(), t, I_SHARED,
+            sh.gate.data_ptr(), sh.up.data_ptr(), sh.down.data_ptr(), y.data_ptr(), ys.data_ptr(), wsb.data_ptr(),
+            nbytes, L.status_word(dev).data_ptr(), stream.cuda_stream)
+        L.check(rc, "moe_expert_ffn_grouped")
 
     n = 50
     ms1 = time_loop(lambda: part(1), n, 5, 1, stream)

@@ -58,8 +58,10 @@ _SIGNATURES = {
     "moe_status_string": ([_i32], ctypes.c_char_p),
     "moe_last_error": ([], ctypes.c_char_p),
     "moe_device_sm_count": ([], _i32),
+    "moe_route_workspace_bytes": ([_i64, _i64], _sz),
     "moe_route": (
-        [_p, _i32, _p, _i32, _p, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _p, _p, _p, _p, _p],
+        [_p, _i32, _p, _i32, _p, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _p, _p, _p, _p, _sz, _p,
+         _p],
         _i32,
     ),
     "moe_group_workspace_bytes": ([_i64, _i32, _i64], _sz),
@@ -84,8 +86,8 @@ _SIGNATURES = {
         _i32,
     ),
     "moe_expert_ffn_grouped": (
-        [_i32, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _p,
-         _p, _p, _p, _p, _p, _sz, _p, _p],
+        [_i32, _p, _i32, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _i32, _p, _i64,
+         _i64, _p, _p, _p, _p, _p, _p, _sz, _p, _p],
         _i32,
     ),
     "moe_combine": ([_p, _i32, _p, _p, _i64, _i32, _i64, _p, _p, _i32, _p, _p], _i32),

@@ -65,36 +65,93 @@ __device__ __forceinline__ void store8(void* base, int dt, int64_t off, const fl
   }
 }
 
-__global__ void __launch_bounds__(kThreads) combine_kernel(const Params p) {
-  __shared__ int s_pos[kThreads / 32][kMaxK];
-  __shared__ float s_w[kThreads / 32][kMaxK];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp;
-  if (t >= p.T) return;
-  const int64_t rows = p.T * p.k;
-  if (lane < p.k) {
-    int r = p.pos[t * p.k + lane];
-    float w = p.w[t * p.k + lane];
-    if (r < 0 || r >= rows) {
-      // a slot the grouping rejected (or a corrupted position): contributes 0
-      if (p.status && r >= rows) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
-      r = 0;
-      w = 0.f;
-    }
-    s_pos[warp][lane] = r;
-    s_w[warp][lane] = w;
-  }
-  __syncwarp();
-  for (int64_t h = lane * 8; h < p.H; h += 256) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < p.k; ++s) {
-      const int row = s_pos[warp][s];
-      const float ws = s_w[warp][s];
-      float v[8];
-      load8(p.y, p.y_dtype, static_cast<int64_t>(row) * p.H + h, v);
+// 8 consecutive values of a 16-bit row, raw (16 bytes).
+__device__ __forceinline__ uint4 load_raw16(const void* base, int64_t off) {
+  return *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + off);
+}
+
+__device__ __forceinline__ void unpack8(uint4 u, int dt, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(ws, v[i], acc[i]);
+  for (int i = 0; i < 4; ++i) {
+    if (dt == MOE_DT_BF16) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      v[2 * i] = __low2float(h);
+      v[2 * i + 1] = __high2float(h);
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      v[2 * i] = __low2float(h);
+      v[2 * i + 1] = __high2float(h);
     }
+  }
+}
+
+// One warp per (token, run of spw 256-column slices): lane l owns 8 columns of
+// a slice, loads the token's k expert rows (and the shared row) for them
+// kBatch at a time, then sums in slot order. Few tokens: one slice per warp,
+// so a single token is spread over H/256 warps; many tokens: a warp walks
+// several slices of its token.
+constexpr int kBatch = 4;
+
+__global__ void __launch_bounds__(kThreads, 4) combine_kernel(const Params p, int spw) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t slices = (p.H + 255) / 256;
+  const int64_t runs = (slices + spw - 1) / spw;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp;
+  if (unit >= p.T * runs) return;
+  const int64_t t = unit / runs;
+  const int64_t rows = p.T * p.k;
+  int my_r = 0;
+  float my_w = 0.f;
+  if (lane < p.k) {
+    my_r = p.pos[t * p.k + lane];
+    my_w = p.w[t * p.k + lane];
+    if (my_r < 0 || my_r >= rows) {
+      // a slot the grouping rejected (or a corrupted position): contributes 0
+      if (p.status && my_r >= rows) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
+      my_r = 0;
+      my_w = 0.f;
+    }
+  }
+  const bool y16 = p.y_dtype != MOE_DT_F32;
+  const int64_t slice0 = (unit % runs) * spw;
+  for (int64_t sl = slice0; sl < slice0 + spw && sl < slices; ++sl) {
+    const int64_t h = sl * 256 + lane * 8;
+    const bool active = h < p.H;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < p.k; s0 += kBatch) {
+      int r[kBatch];
+      float ws[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        r[j] = __shfl_sync(0xffffffffu, my_r, (s0 + j) & 31);
+        ws[j] = __shfl_sync(0xffffffffu, my_w, (s0 + j) & 31);
+      }
+      if (!active) continue;
+      if (y16) {
+        uint4 raw[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+          if (s0 + j < p.k) raw[j] = load_raw16(p.y, static_cast<int64_t>(r[j]) * p.H + h);
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          if (s0 + j < p.k) {
+            float v[8];
+            unpack8(raw[j], p.y_dtype, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(ws[j], v[i], acc[i]);
+          }
+        }
+      } else {
+        for (int j = 0; j < kBatch && s0 + j < p.k; ++j) {
+          float v[8];
+          load8(p.y, p.y_dtype, static_cast<int64_t>(r[j]) * p.H + h, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = fmaf(ws[j], v[i], acc[i]);
+        }
+      }
+    }
+    if (!active) continue;
     if (p.y_shared) {
       float v[8];
       load8(p.y_shared, p.y_dtype, t * p.H + h, v);

@@ -50,6 +50,7 @@ struct Segment {
   CUtensorMap map_b0;  // 3D {K, N, G}: plain weight, or gate for SwiGLU
   CUtensorMap map_b1;  // 3D up weight (SwiGLU only)
   const int32_t* offsets;  // G+1 row offsets on the device; nullptr = dense
+  const int64_t* gather_rows;  // if set, logical row r of A is row gather_rows[r] of map_a (4-row gathers)
   const void* scale0;      // (G, N) per-channel scales of b0 (int8 only)
   const void* scale1;      // of b1
   void* out;               // (rows, ldo)
@@ -64,6 +65,8 @@ struct Segment {
   int scale_bf16;
   int out_f32;
   int weight_mod;  // group g multiplies weight g % weight_mod (expert-parallel: (rank, expert) groups)
+  int k_splits;    // > 1: K is split into k_splits ranges, each writing an f32 partial slab
+  int64_t split_stride;  // elements between the partial slabs of consecutive K ranges
 };
 
 struct Params {
@@ -92,7 +95,7 @@ __host__ __device__ __forceinline__ int out_cols_per_tile(const Segment& s) {
 }
 
 struct Tile {
-  int seg, group, widx, row0, rows, n_tile;
+  int seg, group, widx, row0, rows, n_tile, split, kb0, kb1;
 };
 
 __device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
@@ -104,6 +107,14 @@ __device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int 
   const Segment& S = p.seg[s];
   const int oc = out_cols_per_tile(S);
   const int nt = (S.n + oc - 1) / oc;
+  // split-K: the segment's tile list repeats once per K range
+  const int per_split = c.mt[s][S.groups] * nt;
+  const int split = t / per_split;
+  t -= split * per_split;
+  const int nkb = (S.k + BK - 1) / BK;
+  tl.split = split;
+  tl.kb0 = split * nkb / S.k_splits;
+  tl.kb1 = (split + 1) * nkb / S.k_splits;
   int lo = 0, hi = S.groups;  // largest g in [0, G) with mt[g] * nt <= t
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -257,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     bad = __any_sync(0xffffffffu, bad);
     if (lane == 0) {
       const int oc = out_cols_per_tile(Sg);
-      c.seg_tiles[s] = bad ? 0 : running * ((Sg.n + oc - 1) / oc);
+      c.seg_tiles[s] = bad ? 0 : running * ((Sg.n + oc - 1) / oc) * Sg.k_splits;
       if (bad && p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
     }
   }
@@ -270,12 +281,16 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // Lane 0 waits, arms the stage barrier and loads B (and a tiled A); in a
+    // gather segment every lane also loads 4 of the tile's 128 A rows.
     if (lane == 0) {
       for (int s = 0; s < p.num_segs; ++s) {
         tma_prefetch_desc(&p.seg[s].map_a);
         tma_prefetch_desc(&p.seg[s].map_b0);
         if (p.seg[s].swiglu) tma_prefetch_desc(&p.seg[s].map_b1);
       }
+    }
+    {
       uint32_t stage = 0, phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
@@ -283,26 +298,43 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         Tile tl;
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
-        const int nkb = (Sg.k + BK - 1) / BK;
         const int n0 = tl.n_tile * out_cols_per_tile(Sg);
         const bool q8 = kInt8 && Sg.b_int8;
         const uint32_t row_bytes = q8 ? BK : BK * 2;  // bytes of one weight row in a stage
         const uint32_t b_bytes = static_cast<uint32_t>(Sg.mma_n) * row_bytes;
         const uint32_t half = static_cast<uint32_t>(Sg.mma_n / 2) * row_bytes;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
+        const bool gather = Sg.gather_rows != nullptr;
+        int32_t gr[4] = {0, 0, 0, 0};
+        if (gather) {
+          // rows past the group's end read source row 0; their results are not stored
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = 4 * lane + j;
+            gr[j] = r < tl.rows ? static_cast<int32_t>(Sg.gather_rows[tl.row0 + r]) : 0;
+          }
+        }
+        for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
+          int waited = 1;
+          if (lane == 0) waited = wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status) ? 1 : 0;
+          if (!__shfl_sync(0xffffffffu, waited, 0)) { ok = false; break; }
           uint8_t* a_dst = sA + stage * A_BYTES;
           uint8_t* b_dst = q8 ? sQ + stage * Q_BYTES : sB + stage * B_BYTES;
-          mbar_arrive_expect_tx(&c.full[stage], A_BYTES + b_bytes);
-          tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
-          tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
-          if (Sg.swiglu) tma_load_3d(b_dst + half, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&c.full[stage], A_BYTES + b_bytes);
+            if (!gather) tma_load_2d(a_dst, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
+            tma_load_3d(b_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
+            if (Sg.swiglu) tma_load_3d(b_dst + half, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
+          }
+          if (gather) {
+            __syncwarp();
+            tma_gather4(a_dst + lane * 4 * (BK * 2), &Sg.map_a, &c.full[stage], kb * BK, gr[0], gr[1], gr[2], gr[3]);
+          }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         // Let every copy this thread started land before the CTA exits.
         for (int i = 0; i < S; ++i) {
           if (!(issued_mask & (1u << i))) continue;
@@ -325,12 +357,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         Tile tl;
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
-        const int nkb = (Sg.k + BK - 1) / BK;
         const uint32_t idesc = idesc_f16(BM, Sg.mma_n, p.in_f16 != 0);
         if (!wait_parity_bounded(&c.tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
           if (kInt8 && Sg.b_int8) {
             if (!wait_parity_bounded(&c.conv[stage], (conv_par >> stage) & 1u, abort_flag, p.status)) {
               ok = false;
@@ -347,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             mma_f16_ss(d, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), idesc,
-                       (kb | kk) != 0 ? 1u : 0u);
+                       (kb != tl.kb0 || kk != 0) ? 1u : 0u);
           }
           issued = true;
           mma_commit(&c.empty[stage]);
@@ -376,9 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         Tile tl;
         decode_tile(c, p, t, tl);
         const Segment& Sg = p.seg[tl.seg];
-        const int nkb = (Sg.k + BK - 1) / BK;
         const int items = Sg.mma_n * 4;  // 16-byte int8 chunks in one stage
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
           if (Sg.b_int8) {
             if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) { ok = false; break; }
             const uint8_t* q = sQ + stage * Q_BYTES;
@@ -412,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       const bool valid = r < tl.rows;
-      const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo;
+      const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo + tl.split * Sg.split_stride;
       const bool vec_ok = (Sg.ldo % 8) == 0;
       const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
       const int oc = out_cols_per_tile(Sg);

@@ -131,14 +131,14 @@ __global__ void __launch_bounds__(kThreads) group_scatter_kernel(const Params p)
       if (e < p.E) {
         const int off = running + v - cnt;
         base[e] += off;
-        if (c == 0) {
+        if (c == 0 && blockIdx.y == 0) {
           p.counts[e] = cnt;
           p.offsets[e] = off;
         }
       }
       running += __shfl_sync(0xffffffffu, v, 31);
     }
-    if (c == 0 && lane == 0) p.offsets[p.E] = running;
+    if (c == 0 && lane == 0 && blockIdx.y == 0) p.offsets[p.E] = running;
   }
   __syncthreads();
   const int64_t f = static_cast<int64_t>(c) * kChunk + tid;
@@ -153,23 +153,61 @@ __global__ void __launch_bounds__(kThreads) group_scatter_kernel(const Params p)
   if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
   __syncthreads();
   int row = -1;
+  const bool writer = blockIdx.y == 0;  // copy slices > 0 only gather rows
   if (e >= 0) {
     row = base[e] + rank;
     for (int w = 0; w < warp; ++w) row += wcnt[w][e];
-    p.pos[f] = row;
-    const int64_t tok = f / p.k;
-    if (p.sorted_token_idx) p.sorted_token_idx[row] = tok;
-    if (p.sorted_weight) p.sorted_weight[row] = p.w[f];
-  } else if (f < p.n) {
+    if (writer) {
+      p.pos[f] = row;
+      const int64_t tok = f / p.k;
+      if (p.sorted_token_idx) p.sorted_token_idx[row] = tok;
+      if (p.sorted_weight) p.sorted_weight[row] = p.w[f];
+    }
+  } else if (f < p.n && writer) {
     p.pos[f] = -1;  // invalid id: the histogram pass already raised the status
   }
-  if (p.xs) {
+  if (!p.xs) return;
+  if (p.x_dtype == MOE_DT_F32) {
     for (int i = 0; i < 32; ++i) {
       const int r = __shfl_sync(0xffffffffu, row, i);
       if (r < 0) continue;
       const int64_t fi = static_cast<int64_t>(c) * kChunk + warp * 32 + i;
       copy_row(p, r, fi / p.k, lane);
     }
+    return;
+  }
+  // 16-bit rows: this CTA copies column slice blockIdx.y of its 32 x 8 rows,
+  // eight independent 16-byte loads in flight per lane.
+  __shared__ int s_dst[kThreads / 32][32];
+  __shared__ int s_src[kThreads / 32][32];
+  s_dst[warp][lane] = row;
+  s_src[warp][lane] = row >= 0 ? static_cast<int>(f / p.k) : -1;
+  __syncwarp();
+  const int per_row = static_cast<int>(p.H / 8);
+  const int cols = per_row / static_cast<int>(gridDim.y);
+  const int c0 = static_cast<int>(blockIdx.y) * cols;
+  const int n_items = 32 * cols;
+  const uint4* src = reinterpret_cast<const uint4*>(p.x);
+  uint4* dst = reinterpret_cast<uint4*>(p.xs);
+  for (int b0 = 0; b0 < n_items; b0 += 32 * 8) {
+    uint4 v[8];
+    int64_t to[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = b0 + u * 32 + lane;
+      to[u] = -1;
+      if (i < n_items) {
+        const int r = i / cols, cc = c0 + i % cols;
+        const int s = s_src[warp][r];
+        if (s >= 0) {
+          v[u] = __ldg(src + static_cast<int64_t>(s) * per_row + cc);
+          to[u] = static_cast<int64_t>(s_dst[warp][r]) * per_row + cc;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (to[u] >= 0) dst[to[u]] = v[u];
   }
 }
 

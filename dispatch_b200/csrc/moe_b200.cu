@@ -98,12 +98,12 @@ size_t dt_size(int dt) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // A operand: 2D {K, rows} with row stride lda elements, box {64, 128}.
-int make_map_a(CUtensorMap* m, const void* a, int dt, int64_t rows, int64_t K, int64_t lda) {
+int make_map_a(CUtensorMap* m, const void* a, int dt, int64_t rows, int64_t K, int64_t lda, int box_rows = 128) {
   EncodeTiledFn enc = encoder();
   if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda * 2)};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, dt == MOE_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(a), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -151,11 +151,20 @@ struct SegSpec {
   bool swiglu;
   int mma_n = moe::gemm::BN;  // multiple of 32 (64 for SwiGLU), <= 256
   bool out_f32 = false;
+  // Gathered A: logical row r reads row gather_rows[r] of `a`, which has
+  // gather_src_rows rows (a_rows stays the logical row count).
+  const int64_t* gather_rows = nullptr;
+  int64_t gather_src_rows = 0;
+  // split-K into f32 partial slabs out + s * split_stride (plain f32 segments)
+  int k_splits = 1;
+  int64_t split_stride = 0;
 };
 
 int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   std::memset(s, 0, sizeof(*s));
-  int rc = make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
+  // a gathered A is fetched one row per box, four boxes per tile::gather4
+  int rc = sp.gather_rows ? make_map_a(&s->map_a, sp.a, act_dtype, sp.gather_src_rows, sp.K, sp.lda, 1)
+                          : make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
   if (rc) return rc;
   const int box_rows = sp.swiglu ? sp.mma_n / 2 : sp.mma_n;
   const int64_t gw = sp.Gw > 0 ? sp.Gw : sp.G;
@@ -166,6 +175,7 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
     if (rc) return rc;
   }
   s->offsets = sp.offsets;
+  s->gather_rows = sp.gather_rows;
   s->scale0 = sp.scale0;
   s->scale1 = sp.scale1;
   s->out = sp.out;
@@ -180,6 +190,8 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   s->scale_bf16 = sp.scale_dtype == MOE_DT_BF16 ? 1 : 0;
   s->mma_n = sp.mma_n;
   s->out_f32 = sp.out_f32 ? 1 : 0;
+  s->k_splits = sp.k_splits;
+  s->split_stride = sp.split_stride;
   return MOE_OK;
 }
 
@@ -198,6 +210,8 @@ int check_seg(const SegSpec& sp, int act_dtype) {
   CHECK_ARG(sp.mma_n >= 32 && sp.mma_n <= moe::gemm::BN && sp.mma_n % (sp.swiglu ? 64 : 32) == 0,
             "MMA width %d must be a multiple of %d in [32, 256]", sp.mma_n, sp.swiglu ? 64 : 32);
   CHECK_ARG(!sp.out_f32 || !sp.swiglu, "f32 output is for plain segments");
+  CHECK_ARG(sp.k_splits >= 1 && sp.k_splits <= (sp.K + 63) / 64 && (sp.k_splits == 1 || sp.out_f32),
+            "split-K needs 1 <= splits <= K/64 and an f32 output");
   CHECK_ARG(sp.lda % 8 == 0 && aligned16(sp.a) && aligned16(sp.b0) && (!sp.b1 || aligned16(sp.b1)),
             "operands must be 16-byte aligned with row strides a multiple of 16 bytes");
   if (sp.b_dtype == MOE_DT_I8) {
@@ -222,10 +236,37 @@ int launch_gemm(const moe::gemm::Params& p, int sms, cudaStream_t stream) {
   return MOE_OK;
 }
 
-int run_gemm(const SegSpec* specs, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
+// Upper bound of a segment's tiles: a non-empty group of c rows has
+// ceil(c/128) <= c/128 + 1 tiles, so a segment has at most R/128 + min(G, R).
+int64_t tile_bound(const SegSpec& sp, int mma_n) {
+  const int oc = sp.swiglu ? mma_n / 2 : mma_n;
+  const int64_t mt = sp.offsets ? sp.a_rows / moe::gemm::BM + (sp.G < sp.a_rows ? sp.G : sp.a_rows)
+                                : (sp.a_rows + moe::gemm::BM - 1) / moe::gemm::BM;
+  return mt * ((sp.N + oc - 1) / oc) * sp.k_splits;
+}
+
+int run_gemm(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
   int sms = 0;
   int rc = device_info(&sms);
   if (rc) return rc;
+  SegSpec specs[moe::gemm::kMaxSegs];
+  for (int i = 0; i < nseg; ++i) specs[i] = specs_in[i];
+  // Narrowing the tiles of small launches (a row's result does not depend on
+  // the tile width) was measured slower on B200: the zero-filled 128-row A
+  // boxes then dominate the TMA traffic. Kept off; the loop below only runs
+  // when kNarrowSmallLaunches is set.
+  constexpr bool kNarrowSmallLaunches = false;
+  for (; kNarrowSmallLaunches;) {
+    int64_t total = 0;
+    bool can_halve = true;
+    for (int i = 0; i < nseg; ++i) {
+      total += tile_bound(specs[i], specs[i].mma_n);
+      can_halve &= !specs[i].out_f32 && specs[i].mma_n >= (specs[i].swiglu ? 128 : 64) &&
+                   specs[i].mma_n % (specs[i].swiglu ? 128 : 64) == 0;
+    }
+    if (total >= sms || !can_halve) break;
+    for (int i = 0; i < nseg; ++i) specs[i].mma_n /= 2;
+  }
   moe::gemm::Params p;
   std::memset(&p, 0, sizeof(p));
   bool any_i8 = false;
@@ -236,9 +277,7 @@ int run_gemm(const SegSpec* specs, int nseg, int act_dtype, int32_t* status, cud
     rc = fill_segment(&p.seg[i], specs[i], act_dtype);
     if (rc) return rc;
     any_i8 |= specs[i].b_dtype == MOE_DT_I8;
-    const int oc = specs[i].swiglu ? specs[i].mma_n / 2 : specs[i].mma_n;
-    const int64_t mt = (specs[i].a_rows + moe::gemm::BM - 1) / moe::gemm::BM + (specs[i].offsets ? specs[i].G : 0);
-    tiles_bound += mt * ((specs[i].N + oc - 1) / oc);
+    tiles_bound += tile_bound(specs[i], specs[i].mma_n);
   }
   p.num_segs = nseg;
   p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
@@ -248,8 +287,12 @@ int run_gemm(const SegSpec* specs, int nseg, int act_dtype, int32_t* status, cud
   return any_i8 ? launch_gemm<true>(p, grid, stream) : launch_gemm<false>(p, grid, stream);
 }
 
+// Most K ranges the router's logit GEMM is split into (f32 slabs in the
+// router workspace).
+constexpr int kRouteMaxSplits = 16;
+
 int route_tb(int64_t H, int E, bool computing) {
-  if (!computing) return 16;
+  if (!computing) return moe::route::kWarps;  // one warp per token for the selection
   int tb = 16;
   while (tb > 1 && static_cast<int64_t>(tb) * (H + E) * 4 > 120 * 1024) tb >>= 1;
   return tb;
@@ -282,10 +325,15 @@ int moe_device_sm_count(void) {
   return device_info(&sms) == MOE_OK ? sms : 0;
 }
 
+size_t moe_route_workspace_bytes(int64_t T, int64_t E) {
+  return static_cast<size_t>(kRouteMaxSplits) * static_cast<size_t>(T > 0 ? T : 1) * static_cast<size_t>(E) *
+         sizeof(float);
+}
+
 int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, const float* logits_in, int64_t T,
               int64_t H, int64_t E, int k, int mode, int renorm, const float* e_score_bias, int n_group,
               int topk_group, float routed_scaling, int32_t* topk_idx, float* topk_w, float* logits_out,
-              int32_t* status, void* stream) {
+              void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
   int sms = 0;
   int rc = device_info(&sms);
   if (rc) return rc;
@@ -310,8 +358,18 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   // f32 epilogue (into logits_out), then the selection kernel reads them.
   const bool tensor_logits = !logits_in && is16(x_dtype) && w_dtype == x_dtype && H % 8 == 0 && aligned16(x) &&
                              aligned16(router_w);
+  int n_splits = 1;
   if (tensor_logits) {
-    CHECK_ARG(logits_out, "logits_out (T, E) f32 is required when the logits are computed from bf16/f16 x");
+    CHECK_ARG(workspace && workspace_bytes >= moe_route_workspace_bytes(T, E), "router workspace too small");
+    // Split K so that about one CTA per SM works on the (few) 128-row tiles;
+    // each K range writes an f32 slab and the selection kernel sums the slabs
+    // in order, so the result does not depend on scheduling.
+    const int64_t m_tiles = (T + moe::gemm::BM - 1) / moe::gemm::BM;
+    const int64_t nkb = (H + moe::gemm::BK - 1) / moe::gemm::BK;
+    int64_t splits = sms / m_tiles;
+    if (splits > kRouteMaxSplits) splits = kRouteMaxSplits;
+    if (splits > nkb) splits = nkb;
+    n_splits = static_cast<int>(splits < 1 ? 1 : splits);
     SegSpec sp{};
     sp.a = x;
     sp.a_rows = T;
@@ -322,17 +380,19 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
     sp.N = E;
     sp.K = H;
     sp.offsets = nullptr;
-    sp.out = logits_out;
+    sp.out = workspace;
     sp.ldo = E;
     sp.swiglu = false;
     sp.mma_n = static_cast<int>((E + 31) / 32 * 32);
     sp.out_f32 = true;
+    sp.k_splits = n_splits;
+    sp.split_stride = T * E;
     rc = run_gemm(&sp, 1, x_dtype, status, s);
     if (rc) return rc;
-    logits_in = logits_out;
-    logits_out = nullptr;
+    logits_in = static_cast<const float*>(workspace);
   }
   moe::route::Params p;
+  p.n_splits = n_splits;
   p.x = x;
   p.w = router_w;
   p.logits_in = logits_in;
@@ -416,9 +476,18 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
   p.xs_f16 = xs_dtype == MOE_DT_F16;
   p.hist = static_cast<int32_t*>(workspace);
   p.status = status;
+  // Copies of 16-bit rows are split by column slices over more CTAs so the
+  // gather uses the whole GPU (about two CTAs per SM).
+  unsigned split = 1;
+  if (xs && x_dtype != MOE_DT_F32) {
+    const int64_t per_row = H / 8;
+    while (split < 8 && static_cast<int64_t>(p.nchunks) * split < 2 * sms && per_row % (2 * split) == 0 &&
+           per_row / (2 * split) >= 32)
+      split *= 2;
+  }
   moe::group::group_hist_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
   CUDA_TRY(cudaGetLastError(), "group_hist_kernel launch");
-  moe::group::group_scatter_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
+  moe::group::group_scatter_kernel<<<dim3(p.nchunks, split), moe::group::kThreads, 0, s>>>(p);
   CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
   return MOE_OK;
 }
@@ -557,20 +626,23 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                         const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
                         const void* shared_up, const void* shared_down, void* y, void* y_shared, void* workspace,
                         size_t workspace_bytes, int32_t* status, void* stream) {
-  return moe_expert_ffn_grouped(part, xs, act_dtype, R, H, offsets, E, E, I, gate, up, down, w_dtype, gate_scale,
-                                up_scale, down_scale, scale_dtype, x_shared, T_shared, I_shared, shared_gate,
-                                shared_up, shared_down, y, y_shared, workspace, workspace_bytes, status, stream);
+  return moe_expert_ffn_grouped(part, xs, act_dtype, R, H, offsets, E, E, nullptr, 0, I, gate, up, down, w_dtype,
+                                gate_scale, up_scale, down_scale, scale_dtype, x_shared, T_shared, I_shared,
+                                shared_gate, shared_up, shared_down, y, y_shared, workspace, workspace_bytes, status,
+                                stream);
 }
 
 int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
-                           int64_t G, int64_t E, int64_t I, const void* gate, const void* up, const void* down,
-                           int w_dtype, const void* gate_scale, const void* up_scale, const void* down_scale,
-                           int scale_dtype, const void* x_shared, int64_t T_shared, int64_t I_shared,
-                           const void* shared_gate, const void* shared_up, const void* shared_down, void* y,
-                           void* y_shared, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+                           int64_t G, int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I,
+                           const void* gate, const void* up, const void* down, int w_dtype, const void* gate_scale,
+                           const void* up_scale, const void* down_scale, int scale_dtype, const void* x_shared,
+                           int64_t T_shared, int64_t I_shared, const void* shared_gate, const void* shared_up,
+                           const void* shared_down, void* y, void* y_shared, void* workspace, size_t workspace_bytes,
+                           int32_t* status, void* stream) {
   CHECK_ARG(part >= 1 && part <= 3, "part must be 1 (gate/up), 2 (down) or 3 (both)");
   CHECK_ARG(E >= 1 && G >= E && G % E == 0, "groups G=%lld must be a positive multiple of the experts E=%lld",
             (long long)G, (long long)E);
+  CHECK_ARG(!gather_rows || gather_src_rows >= 1, "gathered rows need the source row count");
   const bool has_shared = T_shared > 0 && x_shared;
   CHECK_ARG(workspace && workspace_bytes >= moe_ffn_workspace_bytes(R, I, has_shared ? T_shared : 0, I_shared),
             "workspace too small");
@@ -588,6 +660,8 @@ int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, i
     a.a = xs; a.a_rows = R; a.lda = H; a.b0 = gate; a.b1 = up; a.b_dtype = w_dtype; a.scale0 = gate_scale;
     a.scale1 = up_scale; a.scale_dtype = scale_dtype; a.G = G; a.Gw = E; a.N = I; a.K = H; a.offsets = offsets;
     a.out = h; a.ldo = I; a.swiglu = true;
+    a.gather_rows = gather_rows;
+    a.gather_src_rows = gather_src_rows;
     SegSpec b{};
     b.a = h; b.a_rows = R; b.lda = I; b.b0 = down; b.b_dtype = w_dtype; b.scale0 = down_scale;
     b.scale_dtype = scale_dtype; b.G = G; b.Gw = E; b.N = H; b.K = I; b.offsets = offsets; b.out = y; b.ldo = H;
@@ -651,8 +725,14 @@ int moe_combine(const void* y, int y_dtype, const int32_t* pos, const float* top
   p.out_dtype = out_dtype;
   p.status = status;
   const int64_t per = moe::combine::kThreads / 32;
-  moe::combine::combine_kernel<<<static_cast<unsigned>((T + per - 1) / per), moe::combine::kThreads, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(p);
+  // Slices of 256 columns per warp: enough warps to cover the GPU (~32 per SM),
+  // but no more, so large batches keep one warp per token.
+  const int64_t slices = (H + 255) / 256;
+  int64_t spw = (T * slices) / (static_cast<int64_t>(sms) * 64);
+  spw = spw < 1 ? 1 : (spw > slices ? slices : spw);
+  const int64_t units = T * ((slices + spw - 1) / spw);
+  moe::combine::combine_kernel<<<static_cast<unsigned>((units + per - 1) / per), moe::combine::kThreads, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(p, static_cast<int>(spw));
   CUDA_TRY(cudaGetLastError(), "combine_kernel launch");
   return MOE_OK;
 }
@@ -693,7 +773,7 @@ LayerWs layer_ws(const MoeLayerDesc* d) {
   const bool shared = d->I_shared > 0;
   size_t o = 0;
   l.idx = o; o += up(R * 4);
-  l.logits = o; o += up(T * static_cast<size_t>(d->E) * 4);
+  l.logits = o; o += up(moe_route_workspace_bytes(d->T, d->E));
   l.w = o; o += up(R * 4);
   l.counts = o; o += up(static_cast<size_t>(d->E) * 4);
   l.offsets = o; o += up(static_cast<size_t>(d->E + 1) * 4);
@@ -738,23 +818,30 @@ int moe_layer_forward(const MoeLayerDesc* d, const void* x, const void* router_w
     wts = const_cast<float*>(topk_w_in);
   } else {
     rc = moe_route(x, d->x_dtype, router_w, d->router_w_dtype, nullptr, d->T, d->H, d->E, d->k, d->router_mode,
-                   d->renorm, e_score_bias, d->n_group, d->topk_group, d->routed_scaling, idx, wts,
-                   reinterpret_cast<float*>(ws + l.logits), status,
-                   stream);
+                   d->renorm, e_score_bias, d->n_group, d->topk_group, d->routed_scaling, idx, wts, nullptr,
+                   ws + l.logits, moe_route_workspace_bytes(d->T, d->E), status, stream);
     if (rc) return rc;
   }
-  rc = moe_group_tokens(idx, MOE_DT_I32, wts, d->T, d->k, d->E, cnt, off, pos, nullptr, nullptr, x, d->x_dtype,
-                        d->H, xs, d->act_dtype, ws + l.group, moe_group_workspace_bytes(d->T, d->k, d->E), status,
-                        stream);
+  // The grouping kernel writes the gathered rows xs (16-byte copies, f32 x
+  // converted on the way). Gathering inside the GEMM with TMA tile::gather4
+  // is supported (moe_expert_ffn_grouped with gather_rows) and bit-identical,
+  // but 128 one-row TMA requests per k-block made the gate/up GEMM 2.5x
+  // slower on B200, so the layer keeps the copy.
+  const bool gather = false;
+  int64_t* sti = gather ? reinterpret_cast<int64_t*>(xs) : nullptr;
+  rc = moe_group_tokens(idx, MOE_DT_I32, wts, d->T, d->k, d->E, cnt, off, pos, sti, nullptr, gather ? nullptr : x,
+                        d->x_dtype, d->H, gather ? nullptr : xs, d->act_dtype, ws + l.group,
+                        moe_group_workspace_bytes(d->T, d->k, d->E), status, stream);
   if (rc) return rc;
-  // The shared expert reads x directly; an f32 x was converted into xs rows
-  // only, so the shared expert needs x in the activation type.
+  // The shared expert reads x directly, so it needs x in the activation type.
   const bool shared = d->I_shared > 0;
   CHECK_ARG(!shared || d->x_dtype == d->act_dtype, "the shared expert needs x in the activation dtype");
-  rc = moe_expert_ffn(xs, d->act_dtype, d->T * d->k, d->H, off, d->E, d->I, gate, up, down, d->w_dtype, gate_scale,
-                      up_scale, down_scale, d->scale_dtype, shared ? x : nullptr, shared ? d->T : 0, d->I_shared,
-                      shared_gate, shared_up, shared_down, y, ys, ws + l.ffn,
-                      moe_ffn_workspace_bytes(d->T * d->k, d->I, shared ? d->T : 0, d->I_shared), status, stream);
+  rc = moe_expert_ffn_grouped(3, gather ? x : xs, d->act_dtype, d->T * d->k, d->H, off, d->E, d->E, sti,
+                              gather ? d->T : 0, d->I, gate, up, down, d->w_dtype, gate_scale, up_scale, down_scale,
+                              d->scale_dtype, shared ? x : nullptr, shared ? d->T : 0, d->I_shared, shared_gate,
+                              shared_up, shared_down, y, ys, ws + l.ffn,
+                              moe_ffn_workspace_bytes(d->T * d->k, d->I, shared ? d->T : 0, d->I_shared), status,
+                              stream);
   if (rc) return rc;
   return moe_combine(y, d->act_dtype, pos, wts, d->T, d->k, d->H, ys, out, d->out_dtype, status, stream);
 }

@@ -30,6 +30,7 @@ struct Params {
   int32_t* status;
   int64_t T, H;
   int E, k, mode, renorm, n_group, topk_group, x_dtype, w_dtype, tb;
+  int n_splits;  // logits_in holds n_splits f32 slabs of (T, E) partial sums, added in order
   float scaling;
 };
 
@@ -102,7 +103,12 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (p.logits_in) {
-    for (int i = threadIdx.x; i < ntok * E; i += kThreads) lg[i] = p.logits_in[t0 * E + i];
+    const int64_t slab = p.T * E;
+    for (int i = threadIdx.x; i < ntok * E; i += kThreads) {
+      float v = p.logits_in[t0 * E + i];
+      for (int s = 1; s < p.n_splits; ++s) v += p.logits_in[s * slab + t0 * E + i];
+      lg[i] = v;
+    }
   } else {
     const int64_t H = p.H;
     for (int64_t i = threadIdx.x; i < static_cast<int64_t>(ntok) * H; i += kThreads)
@@ -153,8 +159,9 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
   for (int t = warp; t < ntok; t += kWarps) {
     const float* l = lg + t * E;
     float v[J];
-    int sel[kMaxK];
-    float wsel[kMaxK];
+    // slot q's expert and weight are kept by lane q
+    int my_sel = 0;
+    float my_w = 0.f;
     if (p.mode == MOE_ROUTER_SOFTMAX) {
 #pragma unroll
       for (int j = 0; j < J; ++j) {
@@ -182,19 +189,17 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
           }
         }
         warp_argmax(bv, bi);
-        sel[q] = bi;
-        wsel[q] = expf(l[bi] - m) / s;
+        if (lane == q) {
+          my_sel = bi;
+          my_w = expf(bv - m) / s;
+        }
         if ((bi & 31) == lane) {
 #pragma unroll
           for (int j = 0; j < J; ++j)
             if (lane + 32 * j == bi) v[j] = -INFINITY;
         }
       }
-      if (p.renorm) {
-        float tot = 0.f;
-        for (int q = 0; q < p.k; ++q) tot += wsel[q];
-        for (int q = 0; q < p.k; ++q) wsel[q] = wsel[q] / tot;
-      }
+      if (p.renorm) my_w = my_w / warp_sum(lane < p.k ? my_w : 0.f);
     } else {
       // sigmoid, group-limited
       float* cb = cbuf[warp];
@@ -246,30 +251,23 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
           }
         }
         warp_argmax(bv, bi);
-        sel[q] = bi;
-        wsel[q] = 1.0f / (1.0f + expf(-l[bi]));
+        if (lane == q) {
+          my_sel = bi;
+          my_w = 1.0f / (1.0f + expf(-l[bi]));
+        }
         if ((bi & 31) == lane) {
 #pragma unroll
           for (int j = 0; j < J; ++j)
             if (lane + 32 * j == bi) v[j] = -INFINITY;
         }
       }
-      if (p.renorm) {
-        float tot = 0.f;
-        for (int q = 0; q < p.k; ++q) tot += wsel[q];
-        for (int q = 0; q < p.k; ++q) wsel[q] = wsel[q] / tot;
-      }
-      for (int q = 0; q < p.k; ++q) wsel[q] *= p.scaling;
+      if (p.renorm) my_w = my_w / warp_sum(lane < p.k ? my_w : 0.f);
+      my_w *= p.scaling;
       __syncwarp();
     }
     if (lane < p.k) {
-      int si = 0;
-      float sw = 0.f;
-      for (int q = 0; q < p.k; ++q)
-        if (q == lane) {
-          si = sel[q];
-          sw = wsel[q];
-        }
+      int si = my_sel;
+      const float sw = my_w;
       if (si < 0 || si >= E) {
         if (p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_EXPERT);
         si = 0;

@@ -127,7 +127,8 @@ class B200Ops:
         ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
         sc = (self.weights.gate.scale, self.weights.up.scale, self.weights.down.scale) if quant else (None,) * 3
         rc = lib.moe_expert_ffn_grouped(
-            3, recv_x.data_ptr() if r else None, L.dt(x), r, h, recv_offsets.data_ptr(), n_groups, self.n_local, i,
+            3, recv_x.data_ptr() if r else None, L.dt(x), r, h, recv_offsets.data_ptr(), n_groups, self.n_local,
+            None, 0, i,
             g.data_ptr(), u.data_ptr(), d.data_ptr(), L.DT_I8 if quant else L.dt(g),
             L.ptr(sc[0]), L.ptr(sc[1]), L.ptr(sc[2]), L.dt(sc[0]) if quant else 0,
             x.data_ptr() if sh is not None else None, t if sh is not None else 0, i_sh,

@@ -138,13 +138,16 @@ def route(
     # the tensor-core logit GEMM writes here (needed whenever x is given)
     lg = torch.empty(t, e, dtype=torch.float32, device=dev) if (return_logits or logits is None) else None
     bias = None if e_score_bias is None else e_score_bias.contiguous().float()
-    rc = L.lib().moe_route(
+    lib = L.lib()
+    ws = None if logits is not None else L.workspace(dev, lib.moe_route_workspace_bytes(t, e), "route")
+    rc = lib.moe_route(
         None if logits is not None else x.data_ptr(), 0 if logits is not None else L.dt(x),
         None if logits is not None else router_weight.data_ptr(), 0 if logits is not None else L.dt(router_weight),
         L.ptr(logits), t, h, e, k,
         L.ROUTER_SIGMOID_GROUP if router.mode == "sigmoid_group" else L.ROUTER_SOFTMAX,
         int(router.renormalize), L.ptr(bias), router.n_group, router.topk_group, router.routed_scaling_factor,
-        idx.data_ptr(), w.data_ptr(), L.ptr(lg), L.status_word(dev).data_ptr(), L.stream_ptr(dev),
+        idx.data_ptr(), w.data_ptr(), L.ptr(lg), L.ptr(ws), 0 if ws is None else ws.numel(),
+        L.status_word(dev).data_ptr(), L.stream_ptr(dev),
     )
     L.check(rc, "route")
     return (idx, w, lg) if return_logits else (idx, w)

@@ -99,21 +99,30 @@ def _stack_and_share(linears: list[torch.nn.Linear]) -> torch.Tensor:
 
 # ---------------------------------------------------------------- fused path
 def expert_ffn(xs: torch.Tensor, offsets: torch.Tensor, weights, shared: SharedExpertWeights | None = None,
-               x_shared: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+               x_shared: torch.Tensor | None = None, *, gather_rows: torch.Tensor | None = None,
+               n_rows: int | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
     """y = down(silu(gate(xs)) * up(xs)) per expert group, and the shared
     expert over x_shared, in two tcgen05 launches. ``weights`` is a
-    StackedExpertWeights (bf16/f16) or a QuantizedStackedExpertWeights."""
+    StackedExpertWeights (bf16/f16) or a QuantizedStackedExpertWeights.
+    With ``gather_rows`` (int64, n_rows entries) routed row r is row
+    gather_rows[r] of ``xs``, fetched by the GEMM's TMA gather instead of a copy."""
     from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights  # noqa: PLC0415
 
     quant = isinstance(weights, QuantizedStackedExpertWeights)
     g, u, d = (weights.gate.data, weights.up.data, weights.down.data) if quant else (weights.gate, weights.up, weights.down)
-    dev = L.require_cuda(xs, offsets, g, u, d, x_shared, what="the B200 expert FFN")
+    dev = L.require_cuda(xs, offsets, g, u, d, x_shared, gather_rows, what="the B200 expert FFN")
     act = xs.dtype
     if act not in (torch.bfloat16, torch.float16):
         raise ValueError(f"dtype mismatch: activations must be bf16/f16, got {act}")
     if not quant and not (g.dtype == u.dtype == d.dtype == act):
         raise ValueError(f"dtype mismatch: x is {act}, expert weights are {g.dtype}")
-    r, h = xs.shape
+    h = xs.shape[1]
+    if gather_rows is not None:
+        if gather_rows.dtype != torch.int64:
+            raise ValueError("gather_rows must be int64")
+        r = int(n_rows if n_rows is not None else gather_rows.numel())
+    else:
+        r = xs.shape[0]
     e, i, _ = g.shape
     if g.shape[2] != h or d.shape[1] != h or d.shape[2] != i:
         raise ValueError(f"K mismatch: x has {h}, weights are gate {tuple(g.shape)} down {tuple(d.shape)}")
@@ -133,8 +142,9 @@ def expert_ffn(xs: torch.Tensor, offsets: torch.Tensor, weights, shared: SharedE
     nbytes = lib.moe_ffn_workspace_bytes(r, i, t_sh, i_sh)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     sc = (weights.gate.scale, weights.up.scale, weights.down.scale) if quant else (None, None, None)
-    rc = lib.moe_expert_ffn(
-        xs.data_ptr(), L.dt(act), r, h, offsets.data_ptr(), e, i,
+    rc = lib.moe_expert_ffn_grouped(
+        3, xs.data_ptr(), L.dt(act), r, h, offsets.data_ptr(), e, e,
+        L.ptr(gather_rows), xs.shape[0] if gather_rows is not None else 0, i,
         g.contiguous().data_ptr(), u.contiguous().data_ptr(), d.contiguous().data_ptr(),
         L.DT_I8 if quant else L.dt(act),
         L.ptr(sc[0]), L.ptr(sc[1]), L.ptr(sc[2]), L.dt(sc[0]) if quant else 0,
@@ -170,10 +180,12 @@ def _routed_forward(x, topk_idx, topk_weight, weights, shared: SharedExpertWeigh
     t, k = topk_idx.shape
     e = weights.num_experts
     x = x.contiguous()
-    _, offsets, pos, _, _, w, xs = _group(topk_idx, topk_weight, e, x=x, xs_dtype=act, want_sorted=False)
     x_sh = None
     if shared is not None:
         x_sh = x if x.dtype == act else x.to(act)
+    # the grouping kernel gathers the rows (a TMA gather inside the GEMM is
+    # available through expert_ffn(gather_rows=...) but measured slower)
+    _, offsets, pos, _, _, w, xs = _group(topk_idx, topk_weight, e, x=x, xs_dtype=act, want_sorted=False)
     y, ys = expert_ffn(xs, offsets, weights, shared, x_sh)
     return combine(y, pos, w.reshape(-1), t, k, ys, out_dtype=x.dtype)
 

@@ -75,14 +75,17 @@ int moe_device_sm_count(void);
  * e_score_bias (E floats, may be NULL), n_group / topk_group, renorm and
  * routed_scaling. When logits_in is non-NULL it is used instead of x/router_w
  * (x and router_w may then be NULL). With bf16/f16 x and a router weight of the
- * same type the logits are a dense tcgen05 GEMM written to logits_out (T, E)
- * f32, which is then required; otherwise (f32 inputs) a CUDA-core kernel
- * computes them and logits_out may be NULL. H must be a multiple of 8.
+ * same type the logits are a dense tcgen05 GEMM, split along K into f32 partial
+ * slabs in the workspace (moe_route_workspace_bytes; the selection sums the
+ * slabs in a fixed order); otherwise (f32 inputs) a CUDA-core kernel computes
+ * them and the workspace may be NULL. logits_out (T, E) f32, may be NULL,
+ * receives the raw gate logits. H must be a multiple of 8.
  */
+size_t moe_route_workspace_bytes(int64_t T, int64_t E);
 int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, const float* logits_in, int64_t T,
               int64_t H, int64_t E, int k, int mode, int renorm, const float* e_score_bias, int n_group,
               int topk_group, float routed_scaling, int32_t* topk_idx, float* topk_w, float* logits_out,
-              int32_t* status, void* stream);
+              void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
  * Token grouping. Replaces group_tokens_by_expert
@@ -176,15 +179,20 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
  * (offsets has G+1 entries) is multiplied by weight g % E, so rows received
  * from R source ranks in (source rank, local expert) order are processed where
  * they landed, with no regrouping copy. Replaces the local compute of
- * make_ep_moe_infer (src/dispatch/kernels/expert_parallel.py:170-178). Other
- * arguments as moe_expert_ffn_part; with G == E it is moe_expert_ffn_part.
+ * make_ep_moe_infer (src/dispatch/kernels/expert_parallel.py:170-178).
+ * gather_rows (R int64, may be NULL): routed row r is read from row
+ * gather_rows[r] of xs, which then has gather_src_rows rows -- the
+ * x[sorted_token_idx] gather of moe_forward.py:72 done by the GEMM's TMA
+ * (tile::gather4) instead of a copy. Other arguments as moe_expert_ffn_part;
+ * with G == E and no gather it is moe_expert_ffn_part.
  */
 int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
-                           int64_t G, int64_t E, int64_t I, const void* gate, const void* up, const void* down,
-                           int w_dtype, const void* gate_scale, const void* up_scale, const void* down_scale,
-                           int scale_dtype, const void* x_shared, int64_t T_shared, int64_t I_shared,
-                           const void* shared_gate, const void* shared_up, const void* shared_down, void* y,
-                           void* y_shared, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+                           int64_t G, int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I,
+                           const void* gate, const void* up, const void* down, int w_dtype, const void* gate_scale,
+                           const void* up_scale, const void* down_scale, int scale_dtype, const void* x_shared,
+                           int64_t T_shared, int64_t I_shared, const void* shared_gate, const void* shared_up,
+                           const void* shared_down, void* y, void* y_shared, void* workspace, size_t workspace_bytes,
+                           int32_t* status, void* stream);
 
 /*
  * Weighted combine / unpermute. Replaces ungroup_and_combine

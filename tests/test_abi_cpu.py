@@ -49,7 +49,8 @@ def test_entry_points_report_missing_device_without_crashing() -> None:
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     lib = L.lib()
-    rc = lib.moe_route(None, 0, None, 0, None, 1, 8, 4, 2, 0, 0, None, 1, 1, 1.0, None, None, None, None, None)
+    rc = lib.moe_route(None, 0, None, 0, None, 1, 8, 4, 2, 0, 0, None, 1, 1, 1.0, None, None, None, None, 0, None,
+                       None)
     assert rc == L.MOE_ERR_NO_DEVICE
     assert b"device" in lib.moe_last_error()
 

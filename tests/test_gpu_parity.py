@@ -88,6 +88,23 @@ def test_grouped_matmul_int8_matches_dequant_oracle(scale_dtype, sizes, n, k) ->
     assert_parity(out, O.grouped_matmul(np32(x), deq, sched.group_offsets))
 
 
+def test_rows_do_not_depend_on_tile_width() -> None:
+    """A small launch uses narrower MMA tiles than a large one; the rows they
+    share must come out byte-identical (the property EP byte-exactness needs)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    e, n, k = 8, 1408, 2048
+    w = randn((e, n, k), g, k ** -0.5)
+    big_sizes = [600, 3, 700, 0, 512, 129, 900, 2]
+    xb = randn((sum(big_sizes), k), g, 1.0)
+    big = grouped_matmul(xb, w, build_tile_schedule(torch.tensor(big_sizes, device=DEV), 16))
+    # two rows of expert 1 and one of expert 7, alone: a handful of tiles -> narrow MMA width
+    rows = [600, 601, sum(big_sizes) - 1]
+    small_sizes = [0, 2, 0, 0, 0, 0, 0, 1]
+    small = grouped_matmul(xb[rows].contiguous(), w, build_tile_schedule(torch.tensor(small_sizes, device=DEV), 16))
+    torch.cuda.synchronize()
+    assert torch.equal(small, big[rows])
+
+
 def test_grouped_matmul_rejects_mismatches() -> None:
     sched = build_tile_schedule(torch.tensor([4], device=DEV), block_m=16)
     x = torch.randn(4, 16, device=DEV, dtype=torch.float16)
@@ -267,6 +284,26 @@ def test_layer_c3_int8_with_bf16_shared(c2_weights: LayerWeights, t: int, scale_
     sh = tuple(np32(s) for s in lw.shared)
     out_ref, _, _ = O.moe_forward(np32(x), None, *deq, 6, shared=sh, topk=(ids, w))
     assert_parity(res.out, out_ref)
+
+
+@pytest.mark.parametrize("t", [1, 300, 2048])
+def test_tma_row_gather_equals_materialized_rows(c2_weights: LayerWeights, t: int) -> None:
+    """The GEMM's tile::gather4 A-load from x must feed the tensor cores the
+    same bytes as the gathered copy: outputs are byte-identical."""
+    from dispatch_b200.kernels.grouping import _group
+    from dispatch_b200.kernels.moe_forward import expert_ffn
+
+    lw = c2_weights
+    g = torch.Generator(device="cuda").manual_seed(300 + t)
+    x = randn((t, 2048), g, 1.0)
+    idx, w = route(x, lw.router, RouterConfig(top_k=6))
+    _, offsets, _, sti, _, _, xs = _group(idx, w, 64, x=x, xs_dtype=torch.bfloat16, want_sorted=True)
+    ws = StackedExpertWeights(lw.gate, lw.up, lw.down)
+    sh = SharedExpertWeights(*lw.shared)
+    y_copy, ys_copy = expert_ffn(xs, offsets, ws, sh, x)
+    y_gath, ys_gath = expert_ffn(x, offsets, ws, sh, x, gather_rows=sti, n_rows=t * 6)
+    assert torch.equal(y_copy, y_gath)
+    assert torch.equal(ys_copy, ys_gath)
 
 
 def test_layer_is_deterministic(c2_weights: LayerWeights) -> None:
