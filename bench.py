@@ -1,17 +1,25 @@
 """MoE-layer throughput on B200: `python bench.py --gpus N --steps K --warmup W`.
 
-Workload (BASELINE config 2 / 4): DeepSeek-V2-Lite-shaped MoE layer, hidden
-2048, 64 routed experts top-6 (softmax router), intermediate 1408 with SwiGLU,
-2 always-on shared experts (intermediate 2816), bf16, T tokens per GPU
-(default 4096, the prefill point), x ~ N(0,1), weights ~ N(0,0.02), seed 0.
-One step = one full layer forward (router -> grouping + gather -> expert FFN
--> combine) through the public API. Weights (1.1 GB) exceed the 126 MB L2, so
-no flush is needed between steps. At N > 1 the 64 experts are sharded
-evenly across ranks (expert parallel), each rank holding T tokens.
+Default workload (and config 4 at N > 1):
+DeepSeek-V2-Lite-shaped MoE layer, hidden 2048, 64 routed experts top-6
+(softmax router), intermediate 1408 with SwiGLU, 2 always-on shared experts
+(intermediate 2816), bf16, T = 4096 tokens per GPU (the prefill point),
+x ~ N(0,1), weights ~ N(0,0.02), seed 0. One step = one full layer forward
+(router -> grouping + gather -> expert FFN -> combine) through the public API.
+The weights (1.1 GB) exceed the 126 MB L2, so no flush is needed between
+steps. At N > 1 the experts are sharded evenly across ranks (expert parallel,
+NCCL all-to-all), each rank holding its own T tokens.
+
+Other configs: `--config c3` (config 3: routed experts int8 weight-only with
+bf16 per-channel scales, shared expert bf16; reports the weight footprint),
+`--config c5` (config 5: DeepSeek-V3-shaped, hidden 7168, 256 experts top-8
+with the sigmoid group-limited router (8 groups, top-4 groups), intermediate
+2048, 1 shared expert, int8 routed experts, T = 8192 per GPU).
 
 `--impl reference` times the reference algorithm's CPU restatement (the
-oracle; the reference is pure PyTorch and cannot travel to the GPU box) on a
-bounded sample of the same workload with all host threads.
+oracle: the reference is pure PyTorch + Triton with no CPU code to compile,
+and cannot travel to the GPU box) on a bounded sample of the same workload
+with all host threads.
 """
 
 from __future__ import annotations
@@ -24,14 +32,60 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-H, E, K_TOP, I, I_SHARED = 2048, 64, 6, 1408, 2816
 METRIC = "MoE-layer tokens/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    desc: str
+    H: int
+    E: int
+    k: int
+    I: int
+    I_s: int
+    tokens: int
+    router: str = "softmax"
+    renorm: bool = False
+    n_group: int = 1
+    topk_group: int = 1
+    scaling: float = 1.0
+    int8: bool = False
+
+    def flops(self, t: int) -> float:
+        """2*T*k*3*H*I + 2*T*3*H*I_s + 2*T*H*E (router)."""
+        return 2.0 * t * self.k * 3 * self.H * self.I + 2.0 * t * 3 * self.H * self.I_s + 2.0 * t * self.H * self.E
+
+    def gateup_flops(self, rows: int, t_shared: int) -> float:
+        return 2.0 * rows * self.H * 2 * self.I + 2.0 * t_shared * self.H * 2 * self.I_s
+
+    def down_flops(self, rows: int, t_shared: int) -> float:
+        return 2.0 * rows * self.I * self.H + 2.0 * t_shared * self.I_s * self.H
+
+    def bytes(self, counts, t: int) -> int:
+        """Active routed weights (+ bf16 scales) + shared + router + x in + out."""
+        active = sum(1 for c in counts if c > 0)
+        wb, sb = (1, 2) if self.int8 else (2, 0)
+        return (active * 3 * self.H * self.I * wb + active * (2 * self.I + self.H) * sb
+                + 3 * self.H * self.I_s * 2 + self.E * self.H * 2 + 2 * t * self.H * 2)
+
+
+WORKLOADS = {
+    "c2": Workload("c2", "C2 DeepSeek-V2-Lite MoE layer (H2048 E64 top6 I1408 + 2 shared), bf16", 2048, 64, 6,
+                   1408, 2816, 4096),
+    "c3": Workload("c3", "C3 DeepSeek-V2-Lite MoE layer, routed experts int8 (bf16 scales), shared bf16", 2048, 64,
+                   6, 1408, 2816, 4096, int8=True),
+    "c5": Workload("c5", "C5 DeepSeek-V3 MoE layer (H7168 E256 top8, sigmoid 8 groups / top-4, I2048 + 1 shared), "
+                   "routed int8", 7168, 256, 8, 2048, 2048, 8192, router="sigmoid_group", renorm=True, n_group=8,
+                   topk_group=4, scaling=2.5, int8=True),
+}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -39,19 +93,6 @@ def load_peaks() -> tuple[dict, str]:
     if p.exists():
         return json.loads(p.read_text()), "measured"
     return PEAKS_FALLBACK, "fallback"
-
-
-def layer_flops(t: int) -> float:
-    return 2.0 * t * K_TOP * 3 * H * I + 2.0 * t * 3 * H * I_SHARED + 2.0 * t * H * E
-
-
-def gateup_flops(rows: int, t_shared: int) -> float:
-    return 2.0 * rows * H * 2 * I + 2.0 * t_shared * H * 2 * I_SHARED
-
-
-def layer_bytes(counts, t: int, w_bytes: int = 2) -> int:
-    active = sum(1 for c in counts if c > 0)
-    return active * 3 * H * I * w_bytes + 3 * H * I_SHARED * 2 + E * H * 2 + t * H * 2 + t * H * 2
 
 
 # ---------------------------------------------------------------- clocks
@@ -142,93 +183,134 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
-# ---------------------------------------------------------------- reference arm
-def run_reference(args) -> None:
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+# ---------------------------------------------------------------- CPU arms
+def oracle_weights(wl: Workload, rng):
+    """f32 weights for the oracle (int8 configs: quantised and dequantised)."""
     import numpy as np
-    from threadpoolctl import threadpool_limits
 
     from oracle import moe_oracle as O
 
+    def f32(*s):
+        w = rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
+        if wl.int8 and len(s) == 3:
+            q, sc = O.quantize_per_channel_int8(w)
+            w = O.dequantize_int8(q, O.round_to_bf16(sc))
+        return w
+
+    gate, up, down = f32(wl.E, wl.I, wl.H), f32(wl.E, wl.I, wl.H), f32(wl.E, wl.H, wl.I)
+    router = f32(wl.E, wl.H)
+    shared = (f32(wl.I_s, wl.H), f32(wl.I_s, wl.H), f32(wl.H, wl.I_s))
+    return router, gate, up, down, shared
+
+
+def oracle_forward(wl: Workload, x, weights):
+    from oracle import moe_oracle as O
+
+    router, gate, up, down, shared = weights
+    return O.moe_forward(x, router, gate, up, down, wl.k, shared=shared, renormalize=wl.renorm)
+
+
+def cpu_sample(wl: Workload, t_sample: int, seconds: float, min_reps: int):
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
     cores = os.cpu_count() or 1
-    t_sample = args.ref_tokens
     rng = np.random.default_rng(0)
-    # Only the experts a sample routes to are touched; all 64 are generated.
-    f32 = lambda *s: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))  # noqa: E731
-    gate, up, down = f32(E, I, H), f32(E, I, H), f32(E, H, I)
-    router = f32(E, H)
-    shared = (f32(I_SHARED, H), f32(I_SHARED, H), f32(H, I_SHARED))
-    x = rng.standard_normal((t_sample, H), dtype=np.float32)
+    weights = oracle_weights(wl, rng)
+    x = rng.standard_normal((t_sample, wl.H), dtype=np.float32)
     times = []
     with threadpool_limits(limits=cores):
-        for step in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            O.moe_forward(x, router, gate, up, down, K_TOP, shared=shared)
-            dt = time.perf_counter() - t0
-            if step >= args.warmup:
-                times.append(dt)
-    sec = statistics.mean(times)
-    value = t_sample / sec
+        oracle_forward(wl, x, weights)
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds or len(times) < min_reps:
+            s = time.perf_counter()
+            oracle_forward(wl, x, weights)
+            times.append(time.perf_counter() - s)
+    return statistics.mean(times), len(times), cores
+
+
+def run_reference(args, wl: Workload) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if wl.name == "c5":
+        print(json.dumps({"impl": "reference", "unavailable": "the f32 CPU oracle of config 5 needs ~45 GB of host "
+                          "memory for its 256 dequantised experts"}), flush=True)
+        return
+    sec, reps, cores = cpu_sample(wl, args.ref_tokens, 0.0, args.warmup + args.steps)
+    value = args.ref_tokens / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"C2 DeepSeek-V2-Lite MoE layer, {t_sample}-token sample of the T={args.tokens} step",
-                   "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "shared_intermediate": I_SHARED,
-                   "tokens_per_gpu": args.tokens, "parallelism": "cpu"},
+        "config": {"workload": f"{wl.desc}; {args.ref_tokens}-token sample of the T={wl.tokens} step",
+                   "tokens_per_gpu": wl.tokens, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{t_sample} tokens x {args.steps} steps of the numpy oracle (f32) forward"},
+                         "sample": f"{args.ref_tokens} tokens x {reps} forwards of the numpy oracle (f32)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample(seconds: float = 12.0) -> dict:
+def cpu_baseline_sample(wl: Workload, seconds: float = 12.0) -> dict:
     """The oracle's forward on a bounded sample, rank 0 / N=1 only."""
-    import numpy as np
-    from threadpoolctl import threadpool_limits
-
-    from oracle import moe_oracle as O
-
-    cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    f32 = lambda *s: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))  # noqa: E731
-    gate, up, down = f32(E, I, H), f32(E, I, H), f32(E, H, I)
-    router = f32(E, H)
-    shared = (f32(I_SHARED, H), f32(I_SHARED, H), f32(H, I_SHARED))
+    if wl.name == "c5":
+        return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": "skipped: the f32 oracle of config 5 needs ~45 GB of host memory"}
     t_sample = 128
-    x = rng.standard_normal((t_sample, H), dtype=np.float32)
-    n = 0
-    with threadpool_limits(limits=cores):
-        O.moe_forward(x, router, gate, up, down, K_TOP, shared=shared)
-        t0 = time.perf_counter()
-        while time.perf_counter() - t0 < seconds or n < 2:
-            O.moe_forward(x, router, gate, up, down, K_TOP, shared=shared)
-            n += 1
-        sec = (time.perf_counter() - t0) / n
+    sec, reps, cores = cpu_sample(wl, t_sample, seconds, 2)
     return {"value": t_sample / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{n} x {t_sample}-token forwards of the numpy oracle (f32, all experts resident)"}
+            "sample": f"{reps} x {t_sample}-token forwards of the numpy oracle (f32, all experts resident)"}
 
 
 # ---------------------------------------------------------------- B200 arm
-def make_inputs(t: int, seed: int, dev):
+def make_inputs(wl: Workload, t: int, seed: int, dev):
+    """Router, experts, shared expert (~N(0, 0.02), seed 0) and x (~N(0,1),
+    seed `seed`). int8 configs quantise the routed experts on the device with
+    bf16 per-channel scales, one chunk of experts at a time."""
     import torch
 
     from dispatch_b200.kernels.moe_forward import SharedExpertWeights, StackedExpertWeights
+    from dispatch_b200.kernels.quantization import (
+        QuantizedStackedExpertWeights,
+        QuantizedTensor,
+        quantize_per_channel_int8,
+    )
 
     g = torch.Generator(device=dev).manual_seed(0)
 
     def rnd(*s, sc=0.02):
         return (torch.randn(*s, generator=g, device=dev) * sc).to(torch.bfloat16)
 
-    router = rnd(E, H)
-    ws = StackedExpertWeights(rnd(E, I, H), rnd(E, I, H), rnd(E, H, I))
-    sh = SharedExpertWeights(rnd(I_SHARED, H), rnd(I_SHARED, H), rnd(H, I_SHARED))
+    def experts(n, kk):
+        if not wl.int8:
+            return rnd(wl.E, n, kk)
+        qs, ss = [], []
+        for e0 in range(0, wl.E, 16):
+            q = quantize_per_channel_int8(rnd(min(16, wl.E - e0), n, kk), scale_dtype=torch.bfloat16)
+            qs.append(q.data)
+            ss.append(q.scale)
+        return QuantizedTensor(torch.cat(qs), torch.cat(ss))
+
+    router = rnd(wl.E, wl.H)
+    gate, up, down = experts(wl.I, wl.H), experts(wl.I, wl.H), experts(wl.H, wl.I)
+    ws = (QuantizedStackedExpertWeights if wl.int8 else StackedExpertWeights)(gate, up, down)
+    sh = SharedExpertWeights(rnd(wl.I_s, wl.H), rnd(wl.I_s, wl.H), rnd(wl.H, wl.I_s))
+    bias = None
+    if wl.router == "sigmoid_group":
+        bias = (torch.randn(wl.E, generator=g, device=dev) * 0.01).float()
     gx = torch.Generator(device=dev).manual_seed(seed)
-    x = torch.randn(t, H, generator=gx, device=dev).to(torch.bfloat16)
-    return x, router, ws, sh
+    x = torch.randn(t, wl.H, generator=gx, device=dev).to(torch.bfloat16)
+    return x, router, ws, sh, bias
+
+
+def weight_footprint(ws) -> int:
+    from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights
+
+    if isinstance(ws, QuantizedStackedExpertWeights):
+        return sum(q.data.numel() * q.data.element_size() + q.scale.numel() * q.scale.element_size()
+                   for q in (ws.gate, ws.up, ws.down))
+    return sum(w.numel() * w.element_size() for w in (ws.gate, ws.up, ws.down))
 
 
 def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
@@ -250,7 +332,7 @@ def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
     return start.elapsed_time(end) / steps
 
 
-def run_b200(args) -> None:
+def run_b200(args, wl: Workload) -> None:
     import torch
 
     from dispatch_b200 import _lib as L
@@ -260,92 +342,99 @@ def run_b200(args) -> None:
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
     peaks, peak_kind = load_peaks()
-    t = args.tokens
-    x, router, ws, sh = make_inputs(t, seed=rank * 1000, dev=dev)
-    cfg = RouterConfig(top_k=K_TOP)
-    bias = None
+    t = args.tokens or wl.tokens
+    x, router, ws, sh, bias = make_inputs(wl, t, seed=rank * 1000, dev=dev)
+    cfg = RouterConfig(top_k=wl.k, mode=wl.router, renormalize=wl.renorm, n_group=wl.n_group,
+                       topk_group=wl.topk_group, routed_scaling_factor=wl.scaling)
     if args.routing == "zipf":
-        import numpy as np
-
-        bias = torch.from_numpy((-1.2 * np.log(np.arange(E) + 1.0)).astype(np.float32)).to(dev)
+        if wl.router != "softmax":
+            raise SystemExit("--routing zipf applies to the softmax-router configs")
+        bias = (-1.2 * torch.log(torch.arange(wl.E, dtype=torch.float32, device=dev) + 1.0))
 
     if world > 1:
         from dispatch_b200.kernels.expert_parallel import EPLayer
 
         ep = EPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias)
-        step = lambda: ep(x)  # noqa: E731
+
+        def layer(xx):
+            return ep(xx)
+
         launches_per_step = ep.launches_per_step
         parallelism = f"ep{world}"
     else:
-        step = lambda: moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)  # noqa: E731
+        def layer(xx):
+            return moe_layer_forward(xx, router, ws, cfg, shared=sh, e_score_bias=bias).out
+
         launches_per_step = 7  # router GEMM + select, group x2, gate/up GEMM, down GEMM, combine
         parallelism = "single"
 
     res = moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)
     torch.cuda.synchronize()
     L.check_device_status(dev)
-    counts = res.group_sizes.cpu().tolist()
 
     with ClockSampler(local) as clocks:
-        ms = time_loop(step, args.steps, args.warmup, world, stream)
+        ms = time_loop(lambda: layer(x), args.steps, args.warmup, world, stream)
     ms = max_over_ranks(ms, world)
     L.check_device_status(dev)
     value = t * world / (ms * 1e-3)
 
     # e2e: the public call with host buffers (pinned), copies inside the timed region
     x_host = x.cpu().pin_memory()
-    out_host = torch.empty(t, H, dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty(t, wl.H, dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty_like(x)
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        out = ep(x_dev) if world > 1 else moe_layer_forward(x_dev, router, ws, cfg, shared=sh, e_score_bias=bias).out
-        out_host.copy_(out, non_blocking=True)
+        out_host.copy_(layer(x_dev), non_blocking=True)
 
     e2e_ms = max_over_ranks(time_loop(e2e_step, max(args.steps // 2, 3), 3, world, stream), world)
     e2e_val = t * world / (e2e_ms * 1e-3)
 
     # dominant kernel: the gate/up tcgen05 GEMM (+SwiGLU epilogue), timed alone
-    roof = gateup_roofline(x, ws, sh, res, peaks, peak_kind, dev, stream)
+    roof = gateup_roofline(wl, x, ws, sh, res, peaks, peak_kind, dev, stream)
 
     sweep = {}
     if world == 1 and not args.no_sweep:
         for tt in (1, 16, 128, 1024):
+            if tt >= t:
+                continue
             xs_ = x[:tt].contiguous()
             r = moe_layer_forward(xs_, router, ws, cfg, shared=sh, e_score_bias=bias)
             torch.cuda.synchronize()
             c = r.group_sizes.cpu().tolist()
             m = time_loop(lambda: moe_layer_forward(xs_, router, ws, cfg, shared=sh, e_score_bias=bias),
                           200, 10, 1, stream)
-            b = layer_bytes(c, tt)
+            b = wl.bytes(c, tt)
             sweep[str(tt)] = {"ms": round(m, 4), "tokens_per_s": round(tt / (m * 1e-3), 1),
                               "hbm_gbs_algorithmic": round(b / (m * 1e-3) / 1e9, 1),
                               "hbm_frac": round(b / (m * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
-        sweep["4096"] = {"ms": round(ms, 4), "tokens_per_s": round(value, 1),
-                         "tflops_algorithmic": round(layer_flops(t) / (ms * 1e-3) / 1e12, 1),
-                         "tensor_frac": round(layer_flops(t) / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
+        sweep[str(t)] = {"ms": round(ms, 4), "tokens_per_s": round(value, 1),
+                         "tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
+                         "tensor_frac": round(wl.flops(t) / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"C2 DeepSeek-V2-Lite MoE layer (H2048 E64 top6 I1408 + 2 shared), "
-                                   f"T={t} tokens/GPU, {args.routing} routing",
-                       "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "shared_intermediate": I_SHARED,
-                       "tokens_per_gpu": t, "global_tokens": t * world, "routing": args.routing,
-                       "parallelism": parallelism, "l2": "inputs larger than L2 (1.1 GB of weights per step)"},
-            "layer_tflops_algorithmic": round(layer_flops(t) / (ms * 1e-3) / 1e12, 1),
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if not wl.int8 else "bf16 x int8",
+            "data": "synthetic",
+            "config": {"workload": f"{wl.desc}, T={t} tokens/GPU, {args.routing} routing",
+                       "hidden": wl.H, "experts": wl.E, "top_k": wl.k, "intermediate": wl.I,
+                       "shared_intermediate": wl.I_s, "router": wl.router, "tokens_per_gpu": t,
+                       "global_tokens": t * world, "routing": args.routing, "parallelism": parallelism,
+                       "routed_weight_bytes": weight_footprint(ws),
+                       "l2": "inputs larger than L2 (expert weights >= 1.1 GB per step)"},
+            "layer_tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
             "roofline": roof,
-            "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s", "h2d_bytes_per_step": t * H * 2,
-                    "d2h_bytes_per_step": t * H * 2},
+            "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s", "h2d_bytes_per_step": t * wl.H * 2,
+                    "d2h_bytes_per_step": t * wl.H * 2},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "sweep": sweep,
             "peaks": {"kind": peak_kind, "hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"]},
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_sample()
+            line["cpu_baseline"] = cpu_baseline_sample(wl)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -353,43 +442,54 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-def gateup_roofline(x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
+# DRAM bytes (read + write) of one gate/up launch on the C2 T=4096 step, from
+# an ncu capture of this kernel (dram__bytes_read.sum + dram__bytes_write.sum).
+GATEUP_TRAFFIC_C2 = 879.5e6 + 68.4e6
+
+
+def gateup_roofline(wl: Workload, x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
     """Times the gate/up GEMM launch alone (CUDA events on its stream) on the
     step's own grouped rows and reports algorithmic TFLOP/s vs the burst peak."""
     import torch
 
     from dispatch_b200 import _lib as L
     from dispatch_b200.kernels.grouping import _group
+    from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights
 
     t = x.shape[0]
-    # the layer's own configuration: routed rows pre-gathered by the grouping kernel
-    _, offsets, _, _, _, _, xs = _group(res.topk_idx, res.topk_weight, E, x=x, xs_dtype=torch.bfloat16,
+    _, offsets, _, _, _, _, xs = _group(res.topk_idx, res.topk_weight, wl.E, x=x, xs_dtype=torch.bfloat16,
                                          want_sorted=False)
     r = xs.shape[0]
+    quant = isinstance(ws, QuantizedStackedExpertWeights)
+    g, u, d = (ws.gate.data, ws.up.data, ws.down.data) if quant else (ws.gate, ws.up, ws.down)
+    sc = (ws.gate.scale, ws.up.scale, ws.down.scale) if quant else (None, None, None)
     lib = L.lib()
-    nbytes = lib.moe_ffn_workspace_bytes(r, I, t, I_SHARED)
+    nbytes = lib.moe_ffn_workspace_bytes(r, wl.I, t, wl.I_s)
     wsb = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    y = torch.empty(r, H, dtype=torch.bfloat16, device=dev)
-    ys = torch.empty(t, H, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(r, wl.H, dtype=torch.bfloat16, device=dev)
+    ys = torch.empty(t, wl.H, dtype=torch.bfloat16, device=dev)
 
     def part(p):
         rc = lib.moe_expert_ffn_grouped(
-            p, xs.data_ptr(), L.DT_BF16, r, H, offsets.data_ptr(), E, E, None, 0, I, ws.gate.data_ptr(),
-            ws.up.data_ptr(), ws.down.data_ptr(), L.DT_BF16, None, None, None, 0, x.data_ptr(), t, I_SHARED,
-            sh.gate.data_ptr(), sh.up.data_ptr(), sh.down.data_ptr(), y.data_ptr(), ys.data_ptr(), wsb.data_ptr(),
-            nbytes, L.status_word(dev).data_ptr(), stream.cuda_stream)
+            p, xs.data_ptr(), L.DT_BF16, r, wl.H, offsets.data_ptr(), wl.E, wl.E, None, 0, wl.I, g.data_ptr(),
+            u.data_ptr(), d.data_ptr(), L.DT_I8 if quant else L.DT_BF16, L.ptr(sc[0]), L.ptr(sc[1]), L.ptr(sc[2]),
+            L.dt(sc[0]) if quant else 0, x.data_ptr(), t, wl.I_s, sh.gate.data_ptr(), sh.up.data_ptr(),
+            sh.down.data_ptr(), y.data_ptr(), ys.data_ptr(), wsb.data_ptr(), nbytes,
+            L.status_word(dev).data_ptr(), stream.cuda_stream)
         L.check(rc, "moe_expert_ffn_grouped")
 
     n = 50
     ms1 = time_loop(lambda: part(1), n, 5, 1, stream)
     ms2 = time_loop(lambda: part(2), n, 5, 1, stream)
-    f1 = gateup_flops(r, t)
+    f1 = wl.gateup_flops(r, t)
     achieved = f1 / (ms1 * 1e-3) / 1e12
-    f2 = 2.0 * r * I * H + 2.0 * t * I_SHARED * H
-    return {"kernel": "grouped_gemm_kernel<bf16> gate/up + SwiGLU (routed + shared)", "bound": "tensor",
+    f2 = wl.down_flops(r, t)
+    traffic = GATEUP_TRAFFIC_C2 if (wl.name == "c2" and t == 4096) else None
+    kernel = "grouped_gemm_kernel<int8> gate/up + SwiGLU" if quant else "grouped_gemm_kernel<bf16> gate/up + SwiGLU"
+    return {"kernel": kernel + " (routed + shared)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 4), "peak_kind": f"{peak_kind} burst",
-            "launch_ms": round(ms1, 4), "flops_per_launch": f1, "traffic": None,
+            "launch_ms": round(ms1, 4), "flops_per_launch": f1, "traffic": traffic,
             "down_gemm": {"launch_ms": round(ms2, 4), "achieved": round(f2 / (ms2 * 1e-3) / 1e12, 1)}}
 
 
@@ -399,7 +499,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: the config's)")
     ap.add_argument("--routing", choices=["uniform", "zipf"], default="uniform")
     ap.add_argument("--ref-tokens", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
@@ -407,10 +508,11 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    wl = WORKLOADS[args.config]
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, wl)
     else:
-        run_b200(args)
+        run_b200(args, wl)
 
 
 if __name__ == "__main__":

@@ -30,19 +30,23 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int BN = 256;  // largest MMA N; TMEM columns per accumulator buffer
-constexpr int kThreads = 256;
 constexpr int kMaxGroups = 256;
 constexpr int kMaxSegs = 2;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB (largest B stage)
 constexpr uint32_t Q_BYTES = BN * BK;      // 16 KiB int8 staging
 constexpr uint32_t kTmemCols = 2 * BN;     // two accumulators of 256 f32 columns
-constexpr int kConvThreads = 64;           // warps 2-3
 
 template <bool kInt8>
 struct Config {
   static constexpr int kStages = kInt8 ? 3 : 4;
   static constexpr uint32_t kStageBytes = A_BYTES + B_BYTES + (kInt8 ? Q_BYTES : 0);
+  // int8 build: six dequantiser warps (2-7) keep up with the MMA; the
+  // epilogue is always the last four warps (one per TMEM lane quarter).
+  static constexpr int kConvWarps = kInt8 ? 6 : 0;
+  static constexpr int kConvThreads = 32 * kConvWarps;
+  static constexpr int kEpiWarp0 = 2 + kConvWarps;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + 4);
 };
 
 struct Segment {
@@ -201,7 +205,7 @@ __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi
 }
 
 template <bool kInt8>
-__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
   using Cfg = Config<kInt8>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -219,13 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
   // ---- setup: group offsets and per-group m-tile prefix in shared memory
   for (int s = 0; s < p.num_segs; ++s) {
     const Segment& Sg = p.seg[s];
-    for (int g = tid; g <= Sg.groups; g += kThreads)
+    for (int g = tid; g <= Sg.groups; g += Cfg::kThreads)
       c.off[s][g] = Sg.offsets ? Sg.offsets[g] : (g == 0 ? 0 : Sg.dense_rows);
   }
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&c.full[i], 1);
-      mbar_init(&c.conv[i], kConvThreads);
+      mbar_init(&c.conv[i], kInt8 ? Cfg::kConvThreads : 1);
       mbar_init(&c.empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
       }
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else if (warp < Cfg::kEpiWarp0) {
     // ------------------------------------------------------------ int8 -> bf16/f16
     if constexpr (kInt8) {
       const int ct = tid - 64;
@@ -413,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) { ok = false; break; }
             const uint8_t* q = sQ + stage * Q_BYTES;
             uint8_t* b = sB + stage * B_BYTES;
-            for (int item = ct; item < items; item += kConvThreads) {
+            for (int item = ct; item < items; item += Cfg::kConvThreads) {
               const int r = item >> 2, cc = item & 3;
               const uint4 v = *reinterpret_cast<const uint4*>(q + r * 64 + cc * 16);
               uint4 lo, hi;

@@ -231,7 +231,7 @@ int launch_gemm(const moe::gemm::Params& p, int sms, cudaStream_t stream) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(gemm)");
-  moe::gemm::grouped_gemm_kernel<kInt8><<<sms, moe::gemm::kThreads, smem, stream>>>(p);
+  moe::gemm::grouped_gemm_kernel<kInt8><<<sms, moe::gemm::Config<kInt8>::kThreads, smem, stream>>>(p);
   CUDA_TRY(cudaGetLastError(), "grouped_gemm_kernel launch");
   return MOE_OK;
 }

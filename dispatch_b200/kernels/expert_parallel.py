@@ -185,6 +185,161 @@ class EPLayer:
         return self.ops.combine(y_back, gr, t, self.top_k, ys, x.dtype)
 
 
+class NcclEPBuffer:
+    """DeepEP V1 ``Buffer``-compatible dispatch/combine over NCCL, so callers
+    written against DeepEP (the reference's ``make_ep_moe_infer``,
+    expert_parallel.py:119-190) run unchanged on ``torch.distributed``.
+
+    Semantics follow the reference's use of DeepEP: tokens go once to each
+    rank that owns at least one of their experts; received top-k ids are
+    local (0..E/R-1) or -1 for slots owned elsewhere; ``combine`` sums the
+    per-rank partial outputs of each token -- here in rank order, in f32,
+    with the deterministic combine kernel (one rounding), instead of DeepEP's
+    unordered reduction.
+    """
+
+    def __init__(self, group=None, *, rank: int | None = None, world: int | None = None):
+        self.group = group
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+
+    def get_dispatch_layout(self, topk_idx: torch.Tensor, num_experts: int):
+        if num_experts % self.world:
+            raise ValueError(f"{num_experts} experts do not split evenly over {self.world} ranks")
+        e_loc = num_experts // self.world
+        valid = topk_idx >= 0
+        dest = torch.where(valid, topk_idx // e_loc, torch.full_like(topk_idx, -1))
+        ranks = torch.arange(self.world, device=topk_idx.device)
+        is_token_in_rank = (dest.unsqueeze(-1) == ranks).any(dim=1)
+        num_tokens_per_rank = is_token_in_rank.sum(0).to(torch.int32)
+        num_tokens_per_expert = torch.bincount(topk_idx[valid].reshape(-1), minlength=num_experts).to(torch.int32)
+        return num_tokens_per_rank, None, num_tokens_per_expert, is_token_in_rank, None
+
+    def dispatch(self, x, topk_idx=None, topk_weights=None, num_tokens_per_rank=None, num_tokens_per_rdma_rank=None,
+                 is_token_in_rank=None, num_tokens_per_expert=None, **_unused):
+        if topk_weights is not None and topk_weights.dtype != torch.float32:
+            raise ValueError("topk_weights must be float32 (DeepEP V1 contract)")
+        e = int(num_tokens_per_expert.numel())
+        e_loc = e // self.world
+        send_idx, send_x, send_topk, send_w, splits = [], [], [], [], []
+        for r in range(self.world):
+            tok = is_token_in_rank[:, r].nonzero(as_tuple=True)[0]
+            local = topk_idx[tok] - r * e_loc
+            owned = (topk_idx[tok] >= 0) & (local >= 0) & (local < e_loc)
+            send_idx.append(tok)
+            send_x.append(x[tok])
+            send_topk.append(torch.where(owned, local, torch.full_like(local, -1)))
+            send_w.append(topk_weights[tok] if topk_weights is not None else None)
+            splits.append(int(tok.numel()))
+        recv_splits = _exchange_splits(splits, x.device, self.group)
+        n_recv = sum(recv_splits)
+        recv_x = x.new_empty(n_recv, x.shape[1])
+        all_to_all_rows(recv_x, torch.cat(send_x), recv_splits, splits, self.group)
+        k = topk_idx.shape[1]
+        recv_topk = topk_idx.new_empty(n_recv, k)
+        all_to_all_rows(recv_topk, torch.cat(send_topk), recv_splits, splits, self.group)
+        recv_w = None
+        if topk_weights is not None:
+            recv_w = topk_weights.new_empty(n_recv, k)
+            all_to_all_rows(recv_w, torch.cat(send_w), recv_splits, splits, self.group)
+        per_expert = torch.bincount(recv_topk[recv_topk >= 0].reshape(-1), minlength=e_loc).tolist()
+        handle = {"send_idx": send_idx, "send_splits": splits, "recv_splits": recv_splits,
+                  "num_tokens": x.shape[0]}
+        return recv_x, recv_topk, recv_w, per_expert, handle, None
+
+    def combine(self, x: torch.Tensor, handle, topk_weights=None, **_unused):
+        splits, recv_splits = handle["send_splits"], handle["recv_splits"]
+        back = x.new_empty(sum(splits), x.shape[1])
+        all_to_all_rows(back, x.contiguous(), splits, recv_splits, self.group)
+        t = handle["num_tokens"]
+        # pos[token, rank] = row of that rank's partial in `back`, -1 if none
+        pos = torch.full((t, self.world), -1, dtype=torch.int32, device=x.device)
+        start = 0
+        for r, idx in enumerate(handle["send_idx"]):
+            pos[idx, r] = torch.arange(start, start + idx.numel(), dtype=torch.int32, device=x.device)
+            start += idx.numel()
+        if back.shape[0] == 0:
+            return torch.zeros(t, x.shape[1], dtype=x.dtype, device=x.device), None, None
+        return self._sum_partials(back, pos, t), None, None
+
+    def _sum_partials(self, back: torch.Tensor, pos: torch.Tensor, t: int) -> torch.Tensor:
+        """out[token] = sum over ranks r (in order) of back[pos[token, r]]: the
+        combine kernel with unit weights (missing partials have pos -1)."""
+        from dispatch_b200.kernels.grouping import combine  # noqa: PLC0415
+
+        ones = (pos >= 0).to(torch.float32)
+        return combine(back, pos.reshape(-1), ones.reshape(-1), t, self.world)
+
+
+def _exchange_splits(splits: list[int], device, group=None) -> list[int]:
+    world = len(splits)
+    send = torch.tensor(splits, dtype=torch.int64, device=device)
+    recv = torch.empty(world, dtype=torch.int64, device=device)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.tolist()
+
+
+def local_expert_contribution(x, topk_idx, topk_weight, local_weights, matmul=None, local_expert_ids=None, *,
+                              block_m: int = 16):
+    """This rank's weighted output for received tokens (reference
+    expert_parallel.py:44-86): slots whose expert is not local get weight 0;
+    ids are remapped to 0..E_local-1 and -1 padding is ignored."""
+    from dispatch_b200.kernels.moe_forward import grouped_moe_routed  # noqa: PLC0415
+
+    n_local = local_weights.num_experts
+    if local_expert_ids is None:
+        local_expert_ids = torch.arange(n_local, device=topk_idx.device)
+    local_expert_ids = local_expert_ids.to(topk_idx.device)
+    is_local = torch.isin(topk_idx, local_expert_ids)
+    span = max(int(local_expert_ids.max().item()), int(topk_idx.max().item()) if topk_idx.numel() else 0) + 1
+    remap = torch.zeros(span, dtype=torch.int64, device=topk_idx.device)
+    remap[local_expert_ids] = torch.arange(n_local, device=topk_idx.device)
+    local_idx = remap[topk_idx.clamp(min=0)]
+    local_w = torch.where(is_local, topk_weight, torch.zeros_like(topk_weight))
+    if x.shape[0] == 0:
+        return x.new_zeros(0, x.shape[1])
+    return grouped_moe_routed(x, local_idx, local_w, local_weights, matmul, block_m=block_m)
+
+
+def make_ep_moe_infer(local_weights, matmul, buffer, num_experts: int, *, block_m: int = 16):
+    """The reference's DeepEP round trip (expert_parallel.py:119-190) on any
+    Buffer-compatible transport (``NcclEPBuffer``)."""
+
+    @torch.no_grad()
+    def moe_infer(x, flat_expert_indices, flat_expert_weights):
+        top_k = flat_expert_indices.numel() // x.shape[0]
+        topk_idx = flat_expert_indices.view(-1, top_k)
+        topk_weight = flat_expert_weights.view(-1, top_k).to(torch.float32)
+        per_rank, per_rdma, per_expert, in_rank, _ = buffer.get_dispatch_layout(topk_idx, num_experts)
+        recv_x, recv_idx, recv_w, _, handle, _ = buffer.dispatch(
+            x, topk_idx=topk_idx, topk_weights=topk_weight, num_tokens_per_rank=per_rank,
+            num_tokens_per_rdma_rank=per_rdma, is_token_in_rank=in_rank, num_tokens_per_expert=per_expert)
+        local_out = local_expert_contribution(recv_x, recv_idx, recv_w.to(x.dtype), local_weights, matmul,
+                                              block_m=block_m)
+        combined, _, _ = buffer.combine(local_out, handle)
+        return combined
+
+    return moe_infer
+
+
+def patch_moe_infer_ep(model: torch.nn.Module, matmul, buffer, rank: int, n_ranks: int, *, block_m: int = 16) -> int:
+    """Each MoE layer's moe_infer computes only this rank's expert shard and
+    exchanges the rest through ``buffer`` (reference expert_parallel.py:193-229)."""
+    from dispatch_b200.kernels.integration import _iter_validated_moe_layers  # noqa: PLC0415
+    from dispatch_b200.kernels.moe_forward import StackedExpertWeights, stack_expert_weights  # noqa: PLC0415
+
+    model.eval()
+    patched = 0
+    for module, experts in _iter_validated_moe_layers(model):
+        n_experts = len(experts)
+        local = (assign_experts_to_ranks(n_experts, n_ranks) == rank).nonzero(as_tuple=True)[0]
+        all_w = stack_expert_weights(experts)
+        local_w = StackedExpertWeights(all_w.gate[local], all_w.up[local], all_w.down[local])
+        module.moe_infer = make_ep_moe_infer(local_w, matmul, buffer, n_experts, block_m=block_m)  # type: ignore[assignment]
+        patched += 1
+    return patched
+
+
 def _slice_experts(weights, lo: int, hi: int):
     from dispatch_b200.kernels.moe_forward import StackedExpertWeights  # noqa: PLC0415
     from dispatch_b200.kernels.quantization import (  # noqa: PLC0415

@@ -18,7 +18,13 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from dispatch_b200.kernels.expert_parallel import EPLayer, Grouped, assign_experts_to_ranks, exchange_layout
+from dispatch_b200.kernels.expert_parallel import (
+    EPLayer,
+    Grouped,
+    NcclEPBuffer,
+    assign_experts_to_ranks,
+    exchange_layout,
+)
 from oracle import moe_oracle as O
 
 H, I, E, K, I_SH, T = 16, 24, 8, 3, 32, 13
@@ -141,6 +147,60 @@ def test_a_rank_that_leaves_makes_the_peer_collective_fail_not_hang(tmp_path) ->
             pytest.fail("a rank did not finish: the failed exchange hung")
     status = (tmp_path / "status0.txt").read_text()
     assert status.startswith("error"), status
+
+
+class CpuSumBuffer(NcclEPBuffer):
+    """The shim with its final partial sum restated on the CPU (the product
+    sums with the CUDA combine kernel)."""
+
+    def _sum_partials(self, back, pos, t):
+        out = torch.zeros(t, back.shape[1])
+        for r in range(self.world):
+            rows = pos[:, r]
+            m = rows >= 0
+            out[m] += back[rows[m].long()]
+        return out
+
+
+def _buffer_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    _init(rank, world, port)
+    try:
+        router, gate, up, down, _ = _weights()
+        x = _tokens(rank)
+        ids, w = O.route_softmax_topk(x @ router.T, K)
+        buf = CpuSumBuffer()
+        idx_t = torch.from_numpy(ids)
+        per_rank, _, per_expert, in_rank, _ = buf.get_dispatch_layout(idx_t, E)
+        assert per_expert.tolist() == np.bincount(ids.ravel(), minlength=E).tolist()
+        recv_x, recv_idx, recv_w, per_local, handle, _ = buf.dispatch(
+            torch.from_numpy(x), topk_idx=idx_t, topk_weights=torch.from_numpy(w), num_tokens_per_rank=per_rank,
+            is_token_in_rank=in_rank, num_tokens_per_expert=per_expert)
+        e_loc = E // world
+        sl = slice(rank * e_loc, (rank + 1) * e_loc)
+        # local contribution of the received tokens (slots owned elsewhere are -1)
+        rx, ri, rw = recv_x.numpy(), recv_idx.numpy(), recv_w.numpy()
+        local = np.zeros_like(rx)
+        for j in range(rx.shape[0]):
+            for s in range(K):
+                if ri[j, s] >= 0:
+                    e = ri[j, s]
+                    local[j] += rw[j, s] * O.swiglu_mlp(rx[j:j + 1], gate[sl][e], up[sl][e], down[sl][e])[0]
+        assert sum(per_local) == int((ri >= 0).sum())
+        combined, _, _ = buf.combine(torch.from_numpy(local), handle)
+        np.save(os.path.join(out_dir, f"buf{rank}.npy"), combined.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_deepep_compatible_buffer_round_trip_matches_routed_forward(tmp_path) -> None:
+    world = 2
+    mp.spawn(_buffer_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    router, gate, up, down, _ = _weights()
+    for r in range(world):
+        x = _tokens(r)
+        ids, w = O.route_softmax_topk(x @ router.T, K)
+        ref = O.grouped_moe_routed(x, ids, w, gate, up, down)
+        np.testing.assert_allclose(np.load(tmp_path / f"buf{r}.npy"), ref, rtol=1e-5, atol=1e-6)
 
 
 def test_exchange_layout_single_rank_is_identity() -> None:

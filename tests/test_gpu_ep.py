@@ -71,6 +71,49 @@ def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str) 
         dist.destroy_process_group()
 
 
+def _buffer_worker(rank: int, world: int, port: int, t: int, out_dir: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from dispatch_b200.kernels.expert_parallel import NcclEPBuffer, _slice_experts, make_ep_moe_infer
+        from dispatch_b200.kernels.layer import RouterConfig, route
+
+        router, ws, _, x = _make(dev, rank, t)
+        idx, w = route(x, router, RouterConfig(top_k=K))
+        e_loc = E // world
+        infer = make_ep_moe_infer(_slice_experts(ws, rank * e_loc, (rank + 1) * e_loc), None, NcclEPBuffer(), E)
+        out = infer(x, idx.long().view(-1), w.view(-1, 1))
+        torch.cuda.synchronize()
+        torch.save({"out": out.cpu(), "idx": idx.cpu(), "w": w.cpu()}, os.path.join(out_dir, f"buf{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_deepep_compatible_buffer_on_two_gpus(tmp_path) -> None:
+    """The reference's make_ep_moe_infer flow on NcclEPBuffer: tolerance parity
+    with the 1-GPU routed layer (the reference's own 2-GPU check is rtol/atol
+    2e-2 against its simulator)."""
+    import torch.multiprocessing as mp
+
+    world, t = NEED, 128
+    mp.spawn(_buffer_worker, args=(world, _free_port(), t, str(tmp_path)), nprocs=world, join=True)
+    from gpu_helpers import assert_parity
+
+    from dispatch_b200.kernels.moe_forward import grouped_moe_routed
+
+    dev = torch.device("cuda", 0)
+    for r in range(world):
+        router, ws, _, x = _make(dev, r, t)
+        got = torch.load(tmp_path / f"buf{r}.pt")
+        ref = grouped_moe_routed(x, got["idx"].to(dev), got["w"].to(dev), ws)
+        assert_parity(got["out"], ref.cpu())
+
+
 @pytest.mark.parametrize("t,skew", [(256, False), (1024, True), (1, False)])
 def test_ep2_output_is_byte_exact_vs_one_gpu(t: int, skew: bool, tmp_path) -> None:
     import torch.multiprocessing as mp
