@@ -361,14 +361,15 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   int n_splits = 1;
   if (tensor_logits) {
     CHECK_ARG(workspace && workspace_bytes >= moe_route_workspace_bytes(T, E), "router workspace too small");
-    // Split K so that about one CTA per SM works on the (few) 128-row tiles;
-    // each K range writes an f32 slab and the selection kernel sums the slabs
-    // in order, so the result does not depend on scheduling.
-    const int64_t m_tiles = (T + moe::gemm::BM - 1) / moe::gemm::BM;
+    // Split K into ranges of 8 k-blocks (512 columns) so that more CTAs work
+    // on the few 128-row tiles; each range writes an f32 slab and the
+    // selection kernel sums the slabs in order. The split depends on H only,
+    // never on T, so a token's logits (and therefore its ids and weights) are
+    // the same bits whatever the batch it is routed in -- which keeps the
+    // expert-parallel output byte-identical to the 1-GPU output.
     const int64_t nkb = (H + moe::gemm::BK - 1) / moe::gemm::BK;
-    int64_t splits = sms / m_tiles;
+    int64_t splits = nkb / 8;
     if (splits > kRouteMaxSplits) splits = kRouteMaxSplits;
-    if (splits > nkb) splits = nkb;
     n_splits = static_cast<int>(splits < 1 ? 1 : splits);
     SegSpec sp{};
     sp.a = x;

@@ -154,6 +154,20 @@ def test_router_fused_logits_c1(x_dtype) -> None:
     np.testing.assert_allclose(w.cpu().numpy(), ww, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("h,e", [(2048, 64), (7168, 256)])
+def test_router_is_batch_invariant(h: int, e: int) -> None:
+    """A token's logits, ids and weights are the same bits whatever batch it
+    is routed in (what keeps EP output byte-identical to the 1-GPU output)."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = randn((2048, h), g, 1.0)
+    w_r = randn((e, h), g, 0.02)
+    cfg = RouterConfig(top_k=8 if e == 256 else 6)
+    ia, wa, la = route(x, w_r, cfg, return_logits=True)
+    for lo, hi in ((0, 1), (5, 133), (1024, 2048)):
+        ib, wb, lb = route(x[lo:hi].contiguous(), w_r, cfg, return_logits=True)
+        assert torch.equal(la[lo:hi], lb) and torch.equal(ia[lo:hi], ib) and torch.equal(wa[lo:hi], wb)
+
+
 def test_sigmoid_group_router_matches_oracle() -> None:
     rng = np.random.default_rng(3)
     logits = rng.standard_normal((512, 256)).astype(np.float32)
