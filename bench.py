@@ -351,16 +351,22 @@ def run_b200(args, wl: Workload) -> None:
             raise SystemExit("--routing zipf applies to the softmax-router configs")
         bias = (-1.2 * torch.log(torch.arange(wl.E, dtype=torch.float32, device=dev) + 1.0))
 
+    ep = None
     if world > 1:
-        from dispatch_b200.kernels.expert_parallel import EPLayer
+        if args.ep_transport == "peer":
+            from dispatch_b200.kernels.ep_peer import PeerEPLayer
 
-        ep = EPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias)
+            ep = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t)
+        else:
+            from dispatch_b200.kernels.expert_parallel import EPLayer
+
+            ep = EPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias)
 
         def layer(xx):
             return ep(xx)
 
         launches_per_step = ep.launches_per_step
-        parallelism = f"ep{world}"
+        parallelism = f"ep{world} ({args.ep_transport})"
     else:
         def layer(xx):
             return moe_layer_forward(xx, router, ws, cfg, shared=sh, e_score_bias=bias).out
@@ -439,6 +445,8 @@ def run_b200(args, wl: Workload) -> None:
     if world > 1:
         import torch.distributed as dist
 
+        if hasattr(ep, "close"):
+            ep.close()
         dist.destroy_process_group()
 
 
@@ -505,6 +513,8 @@ def main() -> None:
     ap.add_argument("--ref-tokens", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="N>1: NVLink peer stores fused into dispatch/FFN (peer) or NCCL all-to-all (nccl)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,4 +1,5 @@
-"""ctypes binding of ``libmoe_b200.so`` (the C ABI in ``include/moe_b200.h``).
+"""ctypes binding of ``libmoe_b200.so`` (the C ABIs in ``include/moe_b200.h``
+and ``include/moe_ep_b200.h``).
 
 The library is built in-tree by ``dispatch_b200.build`` (nvcc, sm_100a). There
 is no fallback: if the library is missing or no sm_100 device is current, every
@@ -98,7 +99,26 @@ _SIGNATURES = {
          _p, _p, _sz, _p, _p],
         _i32,
     ),
+    # include/moe_ep_b200.h
+    "moe_peer_alloc": ([_sz, ctypes.POINTER(_p)], _i32),
+    "moe_peer_free": ([_p], _i32),
+    "moe_peer_export": ([_p, _p], _i32),
+    "moe_peer_import": ([_p, ctypes.POINTER(_p)], _i32),
+    "moe_peer_release": ([_p], _i32),
+    "moe_peer_can_access": ([_i32], _i32),
+    "moe_ep_dispatch": (
+        [_p, _i32, _i64, _i64, _p, _i32, _i32, _p, _p, _p, _i32, _i32, _i64, _p, _p, _i64, _p, _p, _p],
+        _i32,
+    ),
+    "moe_ep_expert_ffn": (
+        [_p, _i32, _i64, _i64, _p, _i64, _p, _p, _i32, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _i32, _p, _i64,
+         _i64, _p, _p, _p, _p, _p, _sz, _p, _p],
+        _i32,
+    ),
 }
+
+PEER_HANDLE_BYTES = 64
+EP_MAX_RANKS = 16
 
 _lib: ctypes.CDLL | None = None
 _lock = threading.Lock()

@@ -71,12 +71,21 @@ struct Segment {
   int weight_mod;  // group g multiplies weight g % weight_mod (expert-parallel: (rank, expert) groups)
   int k_splits;    // > 1: K is split into k_splits ranges, each writing an f32 partial slab
   int64_t split_stride;  // elements between the partial slabs of consecutive K ranges
+  // Scattered output (expert-parallel return): if out_rows is set, logical row
+  // r is stored at row out_rows[r] >> 4 of out_table[out_rows[r] & 15] (a
+  // table of out_table_n bases of out_table_rows rows each, possibly peer
+  // memory) instead of row r of out.
+  const int32_t* out_rows;
+  void* const* out_table;
+  int out_table_n;
+  int64_t out_table_rows;
 };
 
 struct Params {
   Segment seg[kMaxSegs];
   int num_segs;
   int in_f16;  // A/B element type: 0 bf16, 1 f16 (also the 16-bit output type)
+  int remote_out;  // some segment stores through out_table: fence at system scope before exit
   int32_t* status;
 };
 
@@ -445,8 +454,21 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
       if (!wait_parity_bounded(&c.tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      const bool valid = r < tl.rows;
-      const int64_t row_off = static_cast<int64_t>(tl.row0 + r) * Sg.ldo + tl.split * Sg.split_stride;
+      bool valid = r < tl.rows;
+      void* obase = Sg.out;
+      int64_t orow = tl.row0 + r;
+      if (Sg.out_rows && valid) {
+        const int code = Sg.out_rows[orow];
+        const int dst = code & 15;
+        orow = code >> 4;
+        if (code < 0 || dst >= Sg.out_table_n || orow >= Sg.out_table_rows) {
+          if (p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
+          valid = false;
+        } else {
+          obase = Sg.out_table[dst];
+        }
+      }
+      const int64_t row_off = orow * Sg.ldo + tl.split * Sg.split_stride;
       const bool vec_ok = (Sg.ldo % 8) == 0;
       const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
       const int oc = out_cols_per_tile(Sg);
@@ -472,7 +494,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
               }
               h[j] = g / (1.0f + __expf(-g)) * u;
             }
-            store_row32(Sg.out, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
+            store_row32(obase, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
           }
         }
       } else {
@@ -490,7 +512,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
               o[j] = __uint_as_float(v[j]);
               if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
             }
-            store_row32(Sg.out, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
+            store_row32(obase, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
           }
         }
       }
@@ -499,6 +521,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (p.remote_out) __threadfence_system();
   }
 
   tc_fence_before();

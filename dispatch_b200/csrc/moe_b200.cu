@@ -1,5 +1,6 @@
-// Host side of the C ABI declared in include/moe_b200.h: argument checks,
-// TMA tensor-map encoding and kernel launches. No allocation happens here.
+// Host side of the C ABIs declared in include/moe_b200.h and
+// include/moe_ep_b200.h: argument checks, TMA tensor-map encoding and kernel
+// launches. Nothing allocates except the moe_peer_* set-up calls.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -11,7 +12,9 @@
 #include <string>
 
 #include "../../include/moe_b200.h"
+#include "../../include/moe_ep_b200.h"
 #include "combine.cuh"
+#include "ep.cuh"
 #include "gemm.cuh"
 #include "group.cuh"
 #include "route.cuh"
@@ -158,6 +161,11 @@ struct SegSpec {
   // split-K into f32 partial slabs out + s * split_stride (plain f32 segments)
   int k_splits = 1;
   int64_t split_stride = 0;
+  // scattered output rows (Segment::out_rows); out is then unused
+  const int32_t* out_rows = nullptr;
+  void* const* out_table = nullptr;
+  int out_table_n = 0;
+  int64_t out_table_rows = 0;
 };
 
 int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
@@ -192,11 +200,18 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   s->out_f32 = sp.out_f32 ? 1 : 0;
   s->k_splits = sp.k_splits;
   s->split_stride = sp.split_stride;
+  s->out_rows = sp.out_rows;
+  s->out_table = sp.out_table;
+  s->out_table_n = sp.out_table_n;
+  s->out_table_rows = sp.out_table_rows;
   return MOE_OK;
 }
 
 int check_seg(const SegSpec& sp, int act_dtype) {
-  CHECK_ARG(sp.a && sp.b0 && sp.out, "null operand pointer");
+  CHECK_ARG(sp.a && sp.b0 && (sp.out || sp.out_rows), "null operand pointer");
+  CHECK_ARG(!sp.out_rows || (sp.out_table && sp.out_table_n >= 1 && sp.out_table_n <= MOE_EP_MAX_RANKS &&
+                             sp.out_table_rows >= 1 && sp.k_splits == 1 && !sp.out_f32 && sp.ldo % 8 == 0),
+            "scattered output needs a table of 1..%d bases, one K range, 16-bit rows", MOE_EP_MAX_RANKS);
   CHECK_ARG(!sp.swiglu || sp.b1, "null up-projection pointer");
   CHECK_ARG(sp.a_rows > 0 && sp.a_rows < (1ll << 31), "row count %lld out of range", (long long)sp.a_rows);
   CHECK_ARG(sp.G >= 1 && sp.G <= moe::gemm::kMaxGroups, "expert count %lld not in [1, %d]", (long long)sp.G,
@@ -278,6 +293,7 @@ int run_gemm(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, 
     if (rc) return rc;
     any_i8 |= specs[i].b_dtype == MOE_DT_I8;
     tiles_bound += tile_bound(specs[i], specs[i].mma_n);
+    p.remote_out |= specs[i].out_rows ? 1 : 0;
   }
   p.num_segs = nseg;
   p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
@@ -633,13 +649,22 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                                 stream);
 }
 
-int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
-                           int64_t G, int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I,
-                           const void* gate, const void* up, const void* down, int w_dtype, const void* gate_scale,
-                           const void* up_scale, const void* down_scale, int scale_dtype, const void* x_shared,
-                           int64_t T_shared, int64_t I_shared, const void* shared_gate, const void* shared_up,
-                           const void* shared_down, void* y, void* y_shared, void* workspace, size_t workspace_bytes,
-                           int32_t* status, void* stream) {
+// Where the routed down projection stores its rows: y, or scattered through
+// a table of (possibly peer) return buffers.
+struct RoutedOut {
+  const int32_t* rows = nullptr;
+  void* const* table = nullptr;
+  int table_n = 0;
+  int64_t table_rows = 0;
+};
+
+static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets, int64_t G,
+                    int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I, const void* gate,
+                    const void* up, const void* down, int w_dtype, const void* gate_scale, const void* up_scale,
+                    const void* down_scale, int scale_dtype, const void* x_shared, int64_t T_shared,
+                    int64_t I_shared, const void* shared_gate, const void* shared_up, const void* shared_down,
+                    void* y, void* y_shared, void* workspace, size_t workspace_bytes, int32_t* status,
+                    void* stream, const RoutedOut& ro) {
   CHECK_ARG(part >= 1 && part <= 3, "part must be 1 (gate/up), 2 (down) or 3 (both)");
   CHECK_ARG(E >= 1 && G >= E && G % E == 0, "groups G=%lld must be a positive multiple of the experts E=%lld",
             (long long)G, (long long)E);
@@ -667,6 +692,7 @@ int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, i
     b.a = h; b.a_rows = R; b.lda = I; b.b0 = down; b.b_dtype = w_dtype; b.scale0 = down_scale;
     b.scale_dtype = scale_dtype; b.G = G; b.Gw = E; b.N = H; b.K = I; b.offsets = offsets; b.out = y; b.ldo = H;
     b.swiglu = false;
+    b.out_rows = ro.rows; b.out_table = ro.table; b.out_table_n = ro.table_n; b.out_table_rows = ro.table_rows;
     g1[n] = a;
     g2[n] = b;
     ++n;
@@ -688,6 +714,18 @@ int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, i
     if (rc) return rc;
   }
   return (part & 2) ? run_gemm(g2, n, act_dtype, status, s) : MOE_OK;
+}
+
+int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,
+                           int64_t G, int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I,
+                           const void* gate, const void* up, const void* down, int w_dtype, const void* gate_scale,
+                           const void* up_scale, const void* down_scale, int scale_dtype, const void* x_shared,
+                           int64_t T_shared, int64_t I_shared, const void* shared_gate, const void* shared_up,
+                           const void* shared_down, void* y, void* y_shared, void* workspace, size_t workspace_bytes,
+                           int32_t* status, void* stream) {
+  return ffn_impl(part, xs, act_dtype, R, H, offsets, G, E, gather_rows, gather_src_rows, I, gate, up, down, w_dtype,
+                  gate_scale, up_scale, down_scale, scale_dtype, x_shared, T_shared, I_shared, shared_gate, shared_up,
+                  shared_down, y, y_shared, workspace, workspace_bytes, status, stream, RoutedOut{});
 }
 
 int moe_expert_ffn(const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets, int64_t E,
@@ -845,6 +883,132 @@ int moe_layer_forward(const MoeLayerDesc* d, const void* x, const void* router_w
                               stream);
   if (rc) return rc;
   return moe_combine(y, d->act_dtype, pos, wts, d->T, d->k, d->H, ys, out, d->out_dtype, status, stream);
+}
+
+
+// ----------------------------------------------------------------------------
+// Expert-parallel peer exchange (include/moe_ep_b200.h)
+
+static_assert(sizeof(cudaIpcMemHandle_t) == MOE_PEER_HANDLE_BYTES, "IPC handle size");
+
+int moe_peer_alloc(size_t bytes, void** ptr) {
+  CHECK_ARG(ptr && bytes > 0, "null pointer or zero size");
+  *ptr = nullptr;
+  void* p = nullptr;
+  CUDA_TRY(cudaMalloc(&p, bytes), "cudaMalloc(peer buffer)");
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaMemset(peer buffer)");
+  }
+  *ptr = p;
+  return MOE_OK;
+}
+
+int moe_peer_free(void* ptr) {
+  if (!ptr) return MOE_OK;
+  CUDA_TRY(cudaFree(ptr), "cudaFree(peer buffer)");
+  return MOE_OK;
+}
+
+int moe_peer_export(const void* ptr, void* handle) {
+  CHECK_ARG(ptr && handle, "null pointer");
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  return MOE_OK;
+}
+
+int moe_peer_import(const void* handle, void** ptr) {
+  CHECK_ARG(handle && ptr, "null pointer");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return MOE_OK;
+}
+
+int moe_peer_release(void* ptr) {
+  if (!ptr) return MOE_OK;
+  CUDA_TRY(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+  return MOE_OK;
+}
+
+int moe_peer_can_access(int peer) {
+  int dev = 0, ok = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (peer == dev) return 1;
+  if (cudaDeviceCanAccessPeer(&ok, dev, peer) != cudaSuccess) return 0;
+  return ok ? 1 : 0;
+}
+
+int moe_ep_dispatch(const void* x, int x_dtype, int64_t T, int64_t H, const void* topk_idx, int idx_dtype, int k,
+                    const int32_t* pos, const int32_t* offsets, const int32_t* counts_all, int rank, int world,
+                    int64_t E, void* const* peer_recv, int32_t* const* peer_ret, int64_t recv_cap,
+                    int32_t* recv_offsets, int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(world >= 1 && world <= MOE_EP_MAX_RANKS && rank >= 0 && rank < world, "rank %d / world %d out of range",
+            rank, world);
+  CHECK_ARG(E >= world && E <= moe::ep::kMaxE && E % world == 0,
+            "E=%lld must be a multiple of world=%d and at most %d", (long long)E, world, moe::ep::kMaxE);
+  CHECK_ARG(is16(x_dtype), "x must be bf16 or f16");
+  CHECK_ARG(idx_dtype == MOE_DT_I32 || idx_dtype == MOE_DT_I64, "topk_idx must be int32 or int64");
+  CHECK_ARG(k >= 1 && T >= 0 && H % 8 == 0 && H > 0, "bad T/H/k");
+  CHECK_ARG(T * k < (int64_t(1) << 27), "T*k=%lld exceeds the return code's 2^27 rows", (long long)(T * k));
+  CHECK_ARG(recv_cap >= 0 && recv_cap < (int64_t(1) << 31), "recv_cap out of range");
+  CHECK_ARG(counts_all && peer_recv && peer_ret && recv_offsets, "null pointer");
+  CHECK_ARG(T == 0 || (x && topk_idx && pos && offsets), "null pointer");
+  CHECK_ARG(aligned16(x), "x must be 16-byte aligned");
+  moe::ep::DispatchParams p;
+  p.x = x;
+  p.H = H;
+  p.idx = topk_idx;
+  p.idx64 = idx_dtype == MOE_DT_I64;
+  p.n = T * k;
+  p.k = k;
+  p.pos = pos;
+  p.offsets = offsets;
+  p.counts_all = counts_all;
+  p.rank = rank;
+  p.world = world;
+  p.E = static_cast<int>(E);
+  p.e_loc = static_cast<int>(E / world);
+  p.peer_recv = peer_recv;
+  p.peer_ret = peer_ret;
+  p.recv_cap = recv_cap;
+  p.recv_offsets = recv_offsets;
+  p.status = status;
+  // at least one CTA so this rank's receive offsets are written even with no tokens
+  const int64_t chunks = p.n > 0 ? (p.n + moe::ep::kChunk - 1) / moe::ep::kChunk : 1;
+  unsigned split = 1;
+  const int64_t per_row = H / 8;
+  while (split < 8 && chunks * split < 2 * sms && per_row % (2 * split) == 0 && per_row / (2 * split) >= 32)
+    split *= 2;
+  moe::ep::dispatch_kernel<<<dim3(static_cast<unsigned>(chunks), split), moe::ep::kThreads, 0,
+                             static_cast<cudaStream_t>(stream)>>>(p);
+  CUDA_TRY(cudaGetLastError(), "dispatch_kernel launch");
+  return MOE_OK;
+}
+
+int moe_ep_expert_ffn(const void* recv, int act_dtype, int64_t recv_cap, int64_t H, const int32_t* recv_offsets,
+                      int64_t E_loc, const int32_t* recv_ret, void* const* peer_back, int world, int64_t back_rows,
+                      int64_t I, const void* gate, const void* up, const void* down, int w_dtype,
+                      const void* gate_scale, const void* up_scale, const void* down_scale, int scale_dtype,
+                      const void* x_shared, int64_t T_shared, int64_t I_shared, const void* shared_gate,
+                      const void* shared_up, const void* shared_down, void* y_shared, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream) {
+  CHECK_ARG(world >= 1 && world <= MOE_EP_MAX_RANKS, "world %d out of range", world);
+  CHECK_ARG(recv_cap == 0 || (recv && recv_ret && peer_back && back_rows > 0), "null receive/return buffers");
+  RoutedOut ro;
+  ro.rows = recv_ret;
+  ro.table = peer_back;
+  ro.table_n = world;
+  ro.table_rows = back_rows;
+  return ffn_impl(3, recv, act_dtype, recv_cap, H, recv_offsets, E_loc, E_loc, nullptr, 0, I, gate, up, down,
+                  w_dtype, gate_scale, up_scale, down_scale, scale_dtype, x_shared, T_shared, I_shared, shared_gate,
+                  shared_up, shared_down, nullptr, y_shared, workspace, workspace_bytes, status, stream, ro);
 }
 
 }  // extern "C"

@@ -1,0 +1,218 @@
+"""Expert parallelism over NVLink peer memory: the DeepEP round trip of the
+reference's make_ep_moe_infer (src/dispatch/kernels/expert_parallel.py:119-190)
+with every row moved by this library's own kernels (C ABI in
+include/moe_ep_b200.h).
+
+One ``PeerEPLayer`` call on a rank's T local tokens:
+
+1. route and group locally (stable counting sort; no row copy);
+2. NCCL all-gather of the (E,) per-expert counts -> the (world, E) matrix,
+   which fixes every rank's receive layout on every rank;
+3. ``moe_ep_dispatch``: each (token, slot) row is stored by this GPU straight
+   into the receive buffer of the expert's owner, with its return code;
+4. barrier (a 1-element NCCL all-reduce, stream-ordered);
+5. ``moe_ep_expert_ffn``: the grouped SwiGLU FFN over the received rows (and
+   the shared expert over the local tokens, in the same two launches); the
+   down projection's epilogue stores each output row straight into the
+   source rank's return buffer;
+6. barrier;
+7. the weighted combine of the k returned rows per token, in slot order.
+
+No host synchronisation and no staging copies. Every per-row product comes
+from the same kernels with the same per-row arithmetic as the 1-GPU layer and
+the final sum order is the same, so the output is byte-identical to the
+1-GPU result. Buffers are sized for the worst case (every slot of every
+rank's ``max_tokens`` tokens landing on one rank), the way DeepEP's
+low-latency buffers are sized by ``num_max_dispatch_tokens_per_rank``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from dispatch_b200 import _lib as L
+
+
+class PeerBuffers:
+    """One rank's receive rows, return codes and return rows, mapped into
+    every rank of the group through CUDA IPC (no multicast)."""
+
+    def __init__(self, *, rank: int, world: int, group=None, device: torch.device, max_tokens: int, top_k: int,
+                 hidden: int, n_experts: int, act_dtype: torch.dtype = torch.bfloat16):
+        if not 1 <= world <= L.EP_MAX_RANKS:
+            raise ValueError(f"world={world} must be in [1, {L.EP_MAX_RANKS}]")
+        if n_experts % world:
+            raise ValueError(f"{n_experts} experts do not split evenly over {world} ranks")
+        if act_dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("peer exchange moves 16-bit activation rows")
+        self.rank, self.world, self.group = rank, world, group
+        self.device = torch.device(device)
+        self.max_tokens, self.top_k, self.hidden, self.n_experts = max_tokens, top_k, hidden, n_experts
+        self.e_loc = n_experts // world
+        self.act_dtype = act_dtype
+        self.recv_cap = world * max_tokens * min(top_k, self.e_loc)
+        self.back_rows = max_tokens * top_k
+        lib = L.lib()
+        self._lib = lib
+        self._own: list[int] = []
+        self._mapped: list[int] = []
+        dev = self.device
+        with torch.cuda.device(dev):
+            mine = torch.tensor([dev.index], dtype=torch.int32, device=dev)
+            devs = torch.empty(world, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(devs, mine, group=group)
+            bad = [int(d) for d in devs.tolist() if not lib.moe_peer_can_access(int(d))]
+            if bad:
+                raise RuntimeError(f"rank {rank} (cuda:{dev.index}) cannot map the memory of devices {bad}")
+            sizes = (self.recv_cap * hidden * 2, self.recv_cap * 4, self.back_rows * hidden * 2)
+            handles = (ctypes.c_uint8 * (3 * L.PEER_HANDLE_BYTES))()
+            for i, n in enumerate(sizes):
+                p = ctypes.c_void_p()
+                L.check(lib.moe_peer_alloc(n, ctypes.byref(p)), "moe_peer_alloc")
+                self._own.append(p.value)
+                L.check(lib.moe_peer_export(p, ctypes.addressof(handles) + i * L.PEER_HANDLE_BYTES),
+                        "moe_peer_export")
+            local = torch.frombuffer(bytearray(handles), dtype=torch.uint8).to(dev)
+            allh = torch.empty(world * local.numel(), dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(allh, local, group=group)
+            allh = allh.view(world, 3, L.PEER_HANDLE_BYTES).cpu()
+            table = [[0] * world for _ in range(3)]
+            for s in range(world):
+                for i in range(3):
+                    if s == rank:
+                        table[i][s] = self._own[i]
+                        continue
+                    raw = bytes(allh[s, i].tolist())
+                    p = ctypes.c_void_p()
+                    L.check(lib.moe_peer_import(raw, ctypes.byref(p)), "moe_peer_import")
+                    self._mapped.append(p.value)
+                    table[i][s] = p.value
+            self.recv_ptr, self.ret_ptr, self.back_ptr = self._own
+            self.t_recv = torch.tensor(table[0], dtype=torch.int64, device=dev)
+            self.t_ret = torch.tensor(table[1], dtype=torch.int64, device=dev)
+            self.t_back = torch.tensor(table[2], dtype=torch.int64, device=dev)
+            self.counts_all = torch.zeros(world * n_experts, dtype=torch.int32, device=dev)
+            self.recv_offsets = torch.zeros(self.e_loc + 1, dtype=torch.int32, device=dev)
+            self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.barrier()
+            torch.cuda.synchronize(dev)
+
+    def barrier(self) -> None:
+        """Stream-ordered barrier over the group: kernels enqueued after it on
+        any rank run after every rank's kernels enqueued before it."""
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        """Collective: unmaps the peers' buffers and frees this rank's."""
+        if not self._own:
+            return
+        with torch.cuda.device(self.device):
+            self.barrier()
+            torch.cuda.synchronize(self.device)
+            for p in self._mapped:
+                L.check(self._lib.moe_peer_release(p), "moe_peer_release")
+            self._mapped = []
+            self.barrier()
+            torch.cuda.synchronize(self.device)
+            for p in self._own:
+                L.check(self._lib.moe_peer_free(p), "moe_peer_free")
+            self._own = []
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class PeerEPLayer:
+    """Expert-parallel MoE layer for one rank over ``PeerBuffers`` (see the
+    module docstring). Arguments as ``EPLayer``; ``max_tokens`` bounds the
+    tokens per rank of any call."""
+
+    def __init__(self, router_weight, weights, shared, router_cfg, *, rank: int, world: int, group=None,
+                 e_score_bias=None, n_experts: int | None = None, weights_are_local: bool = False,
+                 max_tokens: int = 4096, act_dtype: torch.dtype = torch.bfloat16,
+                 buffers: PeerBuffers | None = None):
+        from dispatch_b200.kernels.expert_parallel import _slice_experts  # noqa: PLC0415
+        from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights  # noqa: PLC0415
+
+        self.rank, self.world, self.group = rank, world, group
+        e = n_experts if n_experts is not None else weights.num_experts * (world if weights_are_local else 1)
+        if e % world:
+            raise ValueError(f"{e} experts do not split evenly over {world} ranks")
+        self.n_experts, self.e_loc = e, e // world
+        if not weights_are_local:
+            weights = _slice_experts(weights, rank * self.e_loc, (rank + 1) * self.e_loc)
+        self.weights, self.shared, self.cfg = weights, shared, router_cfg
+        self.router_weight, self.bias = router_weight, e_score_bias
+        self.top_k = router_cfg.top_k
+        self.quant = isinstance(weights, QuantizedStackedExpertWeights)
+        g = weights.gate.data if self.quant else weights.gate
+        self.hidden, self.inter = g.shape[2], g.shape[1]
+        self.act_dtype = act_dtype
+        self._own_buffers = buffers is None
+        self.buf = buffers or PeerBuffers(rank=rank, world=world, group=group, device=g.device,
+                                          max_tokens=max_tokens, top_k=self.top_k, hidden=self.hidden,
+                                          n_experts=e, act_dtype=self.act_dtype)
+        # launches of this library per call: route x2, group x2, dispatch, FFN x2, combine
+        self.launches_per_step = 8
+
+    def close(self) -> None:
+        if self._own_buffers:
+            self.buf.close()
+
+    @torch.no_grad()
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        from dispatch_b200.kernels.grouping import _group  # noqa: PLC0415
+        from dispatch_b200.kernels.layer import route  # noqa: PLC0415
+
+        dev = L.require_cuda(x, what="expert-parallel layer")
+        t, h = x.shape
+        buf = self.buf
+        if t > buf.max_tokens:
+            raise ValueError(f"{t} tokens exceed the {buf.max_tokens} tokens per rank the peer buffers hold")
+        if h != self.hidden or x.dtype != buf.act_dtype:
+            raise ValueError(f"x must be ({t}, {self.hidden}) {buf.act_dtype}, got {tuple(x.shape)} {x.dtype}")
+        x = x.contiguous()
+        lib = L.lib()
+        st = L.status_word(dev).data_ptr()
+        stream = L.stream_ptr(dev)
+        k = self.top_k
+        idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
+        counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
+        dist.all_gather_into_tensor(buf.counts_all, counts, group=self.group)
+        rc = lib.moe_ep_dispatch(
+            x.data_ptr(), L.dt(x), t, h, idx.data_ptr(), L.dt(idx), k, pos.data_ptr(), offsets.data_ptr(),
+            buf.counts_all.data_ptr(), self.rank, self.world, self.n_experts, buf.t_recv.data_ptr(),
+            buf.t_ret.data_ptr(), buf.recv_cap, buf.recv_offsets.data_ptr(), st, stream,
+        )
+        L.check(rc, "moe_ep_dispatch")
+        buf.barrier()
+        sh = self.shared
+        i_sh = 0 if sh is None else sh.gate.shape[0]
+        ys = torch.empty(t, h, dtype=x.dtype, device=dev) if sh is not None else None
+        wq = self.weights
+        g, u, d = (wq.gate.data, wq.up.data, wq.down.data) if self.quant else (wq.gate, wq.up, wq.down)
+        sc = (wq.gate.scale, wq.up.scale, wq.down.scale) if self.quant else (None,) * 3
+        nbytes = lib.moe_ffn_workspace_bytes(buf.recv_cap, self.inter, t if sh is not None else 0, i_sh)
+        ws = L.workspace(dev, nbytes, "ep_peer_ffn")
+        rc = lib.moe_ep_expert_ffn(
+            buf.recv_ptr, L.dt(x), buf.recv_cap, h, buf.recv_offsets.data_ptr(), self.e_loc, buf.ret_ptr,
+            buf.t_back.data_ptr(), self.world, buf.back_rows, self.inter,
+            g.data_ptr(), u.data_ptr(), d.data_ptr(), L.DT_I8 if self.quant else L.dt(g),
+            L.ptr(sc[0]), L.ptr(sc[1]), L.ptr(sc[2]), L.dt(sc[0]) if self.quant else 0,
+            x.data_ptr() if sh is not None else None, t if sh is not None else 0, i_sh,
+            L.ptr(None if sh is None else sh.gate), L.ptr(None if sh is None else sh.up),
+            L.ptr(None if sh is None else sh.down), L.ptr(ys), ws.data_ptr(), ws.numel(), st, stream,
+        )
+        L.check(rc, "moe_ep_expert_ffn")
+        buf.barrier()
+        out = torch.empty(t, h, dtype=x.dtype, device=dev)
+        rc = lib.moe_combine(buf.back_ptr, L.dt(x), pos.data_ptr(), wf.data_ptr(), t, k, h, L.ptr(ys),
+                             out.data_ptr(), L.dt(out), st, stream)
+        L.check(rc, "moe_combine")
+        return out

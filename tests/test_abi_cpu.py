@@ -17,14 +17,15 @@ ROOT = Path(__file__).resolve().parents[1]
 
 
 def declared_symbols() -> list[str]:
-    text = (ROOT / "include" / "moe_b200.h").read_text()
+    text = "\n".join(h.read_text() for h in sorted((ROOT / "include").glob("*.h")))
     return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(moe_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_entry_points() -> None:
     syms = declared_symbols()
     for must in ("moe_route", "moe_group_tokens", "moe_grouped_gemm", "moe_expert_ffn", "moe_combine",
-                 "moe_quantize_int8", "moe_layer_forward"):
+                 "moe_quantize_int8", "moe_layer_forward", "moe_peer_alloc", "moe_peer_import", "moe_ep_dispatch",
+                 "moe_ep_expert_ffn"):
         assert must in syms
 
 

@@ -1,7 +1,8 @@
-"""Expert parallelism on real GPUs: the EP layer over NCCL on 2 ranks must
-reproduce the 1-GPU layer byte for byte (the 64 experts of
-the DeepSeek-V2-Lite-shaped layer split over the ranks, uniform and Zipf
-routing). Needs at least 2 GPUs; NVLS is off, as in the reference's setup."""
+"""Expert parallelism on real GPUs: the EP layer over NCCL all-to-all and the
+EP layer over NVLink peer memory must reproduce the 1-GPU layer byte for byte
+(the 64 experts of the DeepSeek-V2-Lite-shaped layer split over the ranks,
+uniform and Zipf routing; bf16 and int8 experts). Needs at least 2 GPUs; the
+peer-memory cases also run on every GPU present (up to 8). NVLS is off."""
 
 from __future__ import annotations
 
@@ -46,7 +47,8 @@ def _bias(dev, skew: bool):
     return (-1.2 * torch.log(torch.arange(E, dtype=torch.float32) + 1.0)).to(dev)
 
 
-def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str) -> None:
+def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str, transport: str = "nccl",
+            quant: bool = False) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -58,14 +60,27 @@ def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str) 
         from dispatch_b200.kernels.expert_parallel import EPLayer
         from dispatch_b200.kernels.layer import RouterConfig
 
+        from dispatch_b200.kernels.ep_peer import PeerEPLayer
+
         router, ws, sh, x = _make(dev, rank, t)
-        layer = EPLayer(router, ws, sh, RouterConfig(top_k=K), rank=rank, world=world, e_score_bias=_bias(dev, skew))
+        if quant:
+            from dispatch_b200.kernels.quantization import quantize_stacked_weights
+
+            ws = quantize_stacked_weights(ws)
+        cfg, bias = RouterConfig(top_k=K), _bias(dev, skew)
+        if transport == "peer":
+            layer = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t + 7)
+        else:
+            layer = EPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias)
         out = layer(x)
         out2 = layer(x)  # a second call reuses the same path
+        half = layer(x[: (t + 1) // 2])  # fewer tokens through the same buffers
         torch.cuda.synchronize()
         L.check_device_status(dev)
         assert torch.equal(out, out2)
-        torch.save(out.cpu(), os.path.join(out_dir, f"ep{rank}.pt"))
+        torch.save({"out": out.cpu(), "half": half.cpu()}, os.path.join(out_dir, f"ep{rank}.pt"))
+        if transport == "peer":
+            layer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -114,12 +129,7 @@ def test_deepep_compatible_buffer_on_two_gpus(tmp_path) -> None:
         assert_parity(got["out"], ref.cpu())
 
 
-@pytest.mark.parametrize("t,skew", [(256, False), (1024, True), (1, False)])
-def test_ep2_output_is_byte_exact_vs_one_gpu(t: int, skew: bool, tmp_path) -> None:
-    import torch.multiprocessing as mp
-
-    world = NEED
-    mp.spawn(_worker, args=(world, _free_port(), t, skew, str(tmp_path)), nprocs=world, join=True)
+def _check_byte_exact(tmp_path, world: int, t: int, skew: bool, quant: bool = False) -> None:
     from dispatch_b200.kernels.layer import RouterConfig, moe_layer_forward
 
     dev = torch.device("cuda", 0)
@@ -127,8 +137,40 @@ def test_ep2_output_is_byte_exact_vs_one_gpu(t: int, skew: bool, tmp_path) -> No
     for r in range(world):
         router, ws, sh, x = _make(dev, r, t)
         xs.append(x)
-    ref = moe_layer_forward(torch.cat(xs), router, ws, RouterConfig(top_k=K), shared=sh,
-                            e_score_bias=_bias(dev, skew)).out.cpu()
-    got = torch.cat([torch.load(tmp_path / f"ep{r}.pt") for r in range(world)])
-    assert got.shape == ref.shape
-    assert torch.equal(got, ref), f"max |diff| = {(got.float() - ref.float()).abs().max().item()}"
+    if quant:
+        from dispatch_b200.kernels.quantization import quantize_stacked_weights
+
+        ws = quantize_stacked_weights(ws)
+    fwd = lambda x: moe_layer_forward(x, router, ws, RouterConfig(top_k=K), shared=sh,  # noqa: E731
+                                      e_score_bias=_bias(dev, skew)).out.cpu()
+    got = [torch.load(tmp_path / f"ep{r}.pt") for r in range(world)]
+    for key, ref in (("out", fwd(torch.cat(xs))), ("half", fwd(torch.cat([x[: (t + 1) // 2] for x in xs])))):
+        g = torch.cat([d[key] for d in got])
+        assert g.shape == ref.shape
+        assert torch.equal(g, ref), f"{key}: max |diff| = {(g.float() - ref.float()).abs().max().item()}"
+
+
+@pytest.mark.parametrize("t,skew", [(256, False), (1024, True), (1, False)])
+def test_ep2_output_is_byte_exact_vs_one_gpu(t: int, skew: bool, tmp_path) -> None:
+    import torch.multiprocessing as mp
+
+    world = NEED
+    mp.spawn(_worker, args=(world, _free_port(), t, skew, str(tmp_path)), nprocs=world, join=True)
+    _check_byte_exact(tmp_path, world, t, skew)
+
+
+def _worlds() -> list[int]:
+    n = min(torch.cuda.device_count(), 8)
+    return sorted({NEED, n} | ({4} if n >= 4 else set()))
+
+
+@pytest.mark.parametrize("world", _worlds())
+@pytest.mark.parametrize("t,skew,quant", [(256, False, False), (1024, True, False), (1, False, False),
+                                          (300, True, True)])
+def test_peer_ep_output_is_byte_exact_vs_one_gpu(world: int, t: int, skew: bool, quant: bool, tmp_path) -> None:
+    """Dispatch by NVLink stores, FFN whose epilogue stores the rows back to
+    their source ranks: the same bytes as the 1-GPU layer."""
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(world, _free_port(), t, skew, str(tmp_path), "peer", quant), nprocs=world, join=True)
+    _check_byte_exact(tmp_path, world, t, skew, quant)
