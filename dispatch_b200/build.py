@@ -20,7 +20,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "libmoe_b200.so"
 SOURCES = [CSRC / "moe_b200.cu"]
-DEPS = sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "moe_b200.h"]
+DEPS = sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

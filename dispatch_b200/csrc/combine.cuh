@@ -94,6 +94,8 @@ __device__ __forceinline__ void unpack8(uint4 u, int dt, float (&v)[8]) {
 constexpr int kBatch = 4;
 
 __global__ void __launch_bounds__(kThreads, 4) combine_kernel(const Params p, int spw) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t slices = (p.H + 255) / 256;
   const int64_t runs = (slices + spw - 1) / spw;
@@ -177,6 +179,8 @@ __device__ __forceinline__ float ldf(const void* p, int dt, int64_t i) {
 }
 
 __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantParams p) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp;
   if (r >= p.rows) return;

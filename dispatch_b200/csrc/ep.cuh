@@ -50,6 +50,8 @@ __device__ __forceinline__ int load_id(const DispatchParams& p, int64_t f) {
 }
 
 __global__ void __launch_bounds__(kThreads) dispatch_kernel(const DispatchParams p) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   __shared__ int s_scan[kMaxE + 1];  // exclusive prefix over experts of all sources' rows
   __shared__ int s_pre[kMaxE];       // rows of expert e from sources below this rank
   __shared__ uint4* s_recv[kMaxRanks];

@@ -103,6 +103,10 @@ struct Ctrl {
   int mt[kMaxSegs][kMaxGroups + 1];
 };
 
+// the control block rounded to 16 bytes, then the epilogue's staging (2 KiB per epilogue warp)
+constexpr uint32_t kCtrlBytes = (sizeof(Ctrl) + 15) & ~uint32_t(15);
+constexpr uint32_t kEpiStageBytes = 4 * 32 * 64;
+
 __host__ __device__ __forceinline__ int out_cols_per_tile(const Segment& s) {
   return s.swiglu ? s.mma_n / 2 : s.mma_n;
 }
@@ -193,6 +197,32 @@ __device__ __forceinline__ void store_row32(void* out, int64_t elem_off, const f
   }
 }
 
+// Staged 16-bit store of a warp's 32 x 32 block: lane i holds 32 values of
+// row i; the block goes through 2 KiB of shared memory (16-byte slots XOR-
+// swizzled so both passes are bank-conflict free) and leaves as 8 rows x 64
+// contiguous bytes per store instruction instead of 32 rows x 16 bytes -- a
+// quarter of the write requests, which matters most when the rows live in a
+// peer GPU's memory. rowp[s] is the destination row (element col0) of row
+// s * 8 + lane / 4, or null to skip it.
+__device__ __forceinline__ void store_block32_staged(uint4* stage, const float (&v)[32], int f16, int lane,
+                                                     uint16_t* const (&rowp)[4], int col0) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 pk = make_uint4(pack2(v[q * 8 + 0], v[q * 8 + 1], f16), pack2(v[q * 8 + 2], v[q * 8 + 3], f16),
+                                pack2(v[q * 8 + 4], v[q * 8 + 5], f16), pack2(v[q * 8 + 6], v[q * 8 + 7], f16));
+    stage[lane * 4 + (q ^ ((lane >> 1) & 3))] = pk;
+  }
+  __syncwarp();
+  const int c = lane & 3;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int rr = s * 8 + (lane >> 2);
+    const uint4 val = stage[rr * 4 + (c ^ ((rr >> 1) & 3))];
+    if (rowp[s]) *reinterpret_cast<uint4*>(rowp[s] + col0 + c * 8) = val;
+  }
+  __syncwarp();
+}
+
 // Exact int8 -> 16-bit float for 16 packed bytes. Each signed byte b becomes
 // the f32 2^23 + (b + 128) by byte placement, minus 2^23 + 128.
 __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi) {
@@ -229,12 +259,10 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  // ---- setup: group offsets and per-group m-tile prefix in shared memory
-  for (int s = 0; s < p.num_segs; ++s) {
-    const Segment& Sg = p.seg[s];
-    for (int g = tid; g <= Sg.groups; g += Cfg::kThreads)
-      c.off[s][g] = Sg.offsets ? Sg.offsets[g] : (g == 0 ? 0 : Sg.dense_rows);
-  }
+  // ---- setup: barriers, TMEM and descriptor prefetch (no global memory),
+  // then -- once the previous kernel in the stream is complete -- group
+  // offsets and the per-group m-tile prefix in shared memory
+  pdl_trigger();
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&c.full[i], 1);
@@ -252,6 +280,19 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
   if (warp == 1) {
     tmem_alloc(&c.tmem_base, kTmemCols);
     tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < p.num_segs; ++s) {
+      tma_prefetch_desc(&p.seg[s].map_a);
+      tma_prefetch_desc(&p.seg[s].map_b0);
+      if (p.seg[s].swiglu) tma_prefetch_desc(&p.seg[s].map_b1);
+    }
+  }
+  pdl_wait();
+  for (int s = 0; s < p.num_segs; ++s) {
+    const Segment& Sg = p.seg[s];
+    for (int g = tid; g <= Sg.groups; g += Cfg::kThreads)
+      c.off[s][g] = Sg.offsets ? Sg.offsets[g] : (g == 0 ? 0 : Sg.dense_rows);
   }
   __syncthreads();
   if (warp < p.num_segs) {
@@ -296,13 +337,6 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
     // ------------------------------------------------------------ TMA producer
     // Lane 0 waits, arms the stage barrier and loads B (and a tiled A); in a
     // gather segment every lane also loads 4 of the tile's 128 A rows.
-    if (lane == 0) {
-      for (int s = 0; s < p.num_segs; ++s) {
-        tma_prefetch_desc(&p.seg[s].map_a);
-        tma_prefetch_desc(&p.seg[s].map_b0);
-        if (p.seg[s].swiglu) tma_prefetch_desc(&p.seg[s].map_b1);
-      }
-    }
     {
       uint32_t stage = 0, phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
@@ -446,6 +480,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    uint4* estage = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&c) + kCtrlBytes) + q * 128;
     uint32_t acc = 0, acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       Tile tl;
@@ -473,6 +508,16 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
       const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
       const int oc = out_cols_per_tile(Sg);
       const int n0 = tl.n_tile * oc;
+      // whole 32-column chunks of 16-bit rows go through the staged store
+      const bool staged = !Sg.out_f32 && vec_ok && (Sg.n % 32) == 0;
+      uint16_t* rowp[4];
+      {
+        uint16_t* mine = valid ? reinterpret_cast<uint16_t*>(obase) + row_off : nullptr;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2)
+          rowp[s2] = reinterpret_cast<uint16_t*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(mine), s2 * 8 + (lane >> 2)));
+      }
       if (Sg.swiglu) {
 #pragma unroll 1
         for (int ch = 0; ch < oc / 32; ++ch) {
@@ -481,7 +526,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
           tmem_ld_32x32b_x32(tb + oc + ch * 32, uv);
           tmem_ld_wait();
           const int col0 = n0 + ch * 32;
-          if (valid && col0 < Sg.n) {
+          if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
             const int nc = min(32, Sg.n - col0);
             float h[32];
 #pragma unroll
@@ -494,7 +539,10 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
               }
               h[j] = g / (1.0f + __expf(-g)) * u;
             }
-            store_row32(obase, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
+            if (staged)
+              store_block32_staged(estage, h, p.in_f16, lane, rowp, col0);
+            else
+              store_row32(obase, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
           }
         }
       } else {
@@ -504,7 +552,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
           tmem_ld_32x32b_x32(tb + ch * 32, v);
           tmem_ld_wait();
           const int col0 = n0 + ch * 32;
-          if (valid && col0 < Sg.n) {
+          if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
             const int nc = min(32, Sg.n - col0);
             float o[32];
 #pragma unroll
@@ -512,7 +560,10 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
               o[j] = __uint_as_float(v[j]);
               if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
             }
-            store_row32(obase, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
+            if (staged)
+              store_block32_staged(estage, o, p.in_f16, lane, rowp, col0);
+            else
+              store_row32(obase, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
           }
         }
       }
@@ -534,7 +585,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
 
 template <bool kInt8>
 constexpr size_t smem_bytes() {
-  return 1024 + Config<kInt8>::kStages * Config<kInt8>::kStageBytes + sizeof(Ctrl);
+  return 1024 + Config<kInt8>::kStages * Config<kInt8>::kStageBytes + kCtrlBytes + kEpiStageBytes;
 }
 
 }  // namespace gemm

@@ -50,6 +50,8 @@ __device__ __forceinline__ int load_id(const Params& p, int64_t f) {
 }
 
 __global__ void __launch_bounds__(kThreads) group_hist_kernel(const Params p) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   __shared__ int hist[kMaxE];
   const int tid = threadIdx.x;
   for (int e = tid; e < p.E; e += kThreads) hist[e] = 0;
@@ -97,6 +99,8 @@ __device__ __forceinline__ void copy_row(const Params& p, int64_t dst_row, int64
 }
 
 __global__ void __launch_bounds__(kThreads) group_scatter_kernel(const Params p) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   __shared__ int base[kMaxE];
   __shared__ int total[kMaxE];
   __shared__ int wcnt[kThreads / 32][kMaxE];

@@ -43,6 +43,26 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
 
+// Launches a kernel with programmatic stream serialisation: it may begin its
+// set-up while the previous kernel in the stream drains, and waits for that
+// kernel (griddepcontrol.wait) before touching global memory. Works under
+// stream capture (the graph keeps a programmatic edge).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 #define CHECK_ARG(cond, ...)                                   \
   do {                                                         \
     if (!(cond)) return fail(MOE_ERR_INVALID_ARG, __VA_ARGS__); \
@@ -246,8 +266,9 @@ int launch_gemm(const moe::gemm::Params& p, int sms, cudaStream_t stream) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(gemm)");
-  moe::gemm::grouped_gemm_kernel<kInt8><<<sms, moe::gemm::Config<kInt8>::kThreads, smem, stream>>>(p);
-  CUDA_TRY(cudaGetLastError(), "grouped_gemm_kernel launch");
+  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_kernel<kInt8>, dim3(sms), dim3(moe::gemm::Config<kInt8>::kThreads),
+                      smem, stream, p),
+           "grouped_gemm_kernel launch");
   return MOE_OK;
 }
 
@@ -305,7 +326,7 @@ int run_gemm(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, 
 
 // Most K ranges the router's logit GEMM is split into (f32 slabs in the
 // router workspace).
-constexpr int kRouteMaxSplits = 16;
+constexpr int kRouteMaxSplits = moe::route::kMaxSplits;
 
 int route_tb(int64_t H, int E, bool computing) {
   if (!computing) return moe::route::kWarps;  // one warp per token for the selection
@@ -377,14 +398,15 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   int n_splits = 1;
   if (tensor_logits) {
     CHECK_ARG(workspace && workspace_bytes >= moe_route_workspace_bytes(T, E), "router workspace too small");
-    // Split K into ranges of 8 k-blocks (512 columns) so that more CTAs work
-    // on the few 128-row tiles; each range writes an f32 slab and the
-    // selection kernel sums the slabs in order. The split depends on H only,
-    // never on T, so a token's logits (and therefore its ids and weights) are
-    // the same bits whatever the batch it is routed in -- which keeps the
-    // expert-parallel output byte-identical to the 1-GPU output.
+    // Split K into up to 16 ranges of at least 2 k-blocks so that many CTAs
+    // work on the few 128-row tiles of a small batch (a decode step's logits
+    // are one tile); each range writes an f32 slab and the selection kernel
+    // sums the slabs in order. The split depends on H only, never on T, so a
+    // token's logits (and therefore its ids and weights) are the same bits
+    // whatever the batch it is routed in -- which keeps the expert-parallel
+    // output byte-identical to the 1-GPU output.
     const int64_t nkb = (H + moe::gemm::BK - 1) / moe::gemm::BK;
-    int64_t splits = nkb / 8;
+    int64_t splits = nkb / 2;
     if (splits > kRouteMaxSplits) splits = kRouteMaxSplits;
     n_splits = static_cast<int>(splits < 1 ? 1 : splits);
     SegSpec sp{};
@@ -436,8 +458,9 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
     cudaFuncSetAttribute(moe::route::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
   });
   const int64_t grid = (T + p.tb - 1) / p.tb;
-  moe::route::route_kernel<<<static_cast<unsigned>(grid), moe::route::kThreads, smem, s>>>(p);
-  CUDA_TRY(cudaGetLastError(), "route_kernel launch");
+  CUDA_TRY(launch_pdl(moe::route::route_kernel, dim3(static_cast<unsigned>(grid)), dim3(moe::route::kThreads), smem,
+                      s, p),
+           "route_kernel launch");
   return MOE_OK;
 }
 
@@ -493,18 +516,20 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
   p.xs_f16 = xs_dtype == MOE_DT_F16;
   p.hist = static_cast<int32_t*>(workspace);
   p.status = status;
-  // Copies of 16-bit rows are split by column slices over more CTAs so the
-  // gather uses the whole GPU (about two CTAs per SM).
+  // Copies of 16-bit rows are split by column slices (at least 128 bytes of
+  // a row per CTA) over more CTAs so the gather uses the whole GPU (about two
+  // CTAs per SM) even for a decode step's few rows.
   unsigned split = 1;
   if (xs && x_dtype != MOE_DT_F32) {
     const int64_t per_row = H / 8;
-    while (split < 8 && static_cast<int64_t>(p.nchunks) * split < 2 * sms && per_row % (2 * split) == 0 &&
-           per_row / (2 * split) >= 32)
+    while (split < 32 && static_cast<int64_t>(p.nchunks) * split < 2 * sms && per_row % (2 * split) == 0 &&
+           per_row / (2 * split) >= 8)
       split *= 2;
   }
-  moe::group::group_hist_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
-  CUDA_TRY(cudaGetLastError(), "group_hist_kernel launch");
-  moe::group::group_scatter_kernel<<<dim3(p.nchunks, split), moe::group::kThreads, 0, s>>>(p);
+  CUDA_TRY(launch_pdl(moe::group::group_hist_kernel, dim3(p.nchunks), dim3(moe::group::kThreads), 0, s, p),
+           "group_hist_kernel launch");
+  CUDA_TRY(launch_pdl(moe::group::group_scatter_kernel, dim3(p.nchunks, split), dim3(moe::group::kThreads), 0, s, p),
+           "group_scatter_kernel launch");
   CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
   return MOE_OK;
 }
@@ -770,9 +795,9 @@ int moe_combine(const void* y, int y_dtype, const int32_t* pos, const float* top
   int64_t spw = (T * slices) / (static_cast<int64_t>(sms) * 64);
   spw = spw < 1 ? 1 : (spw > slices ? slices : spw);
   const int64_t units = T * ((slices + spw - 1) / spw);
-  moe::combine::combine_kernel<<<static_cast<unsigned>((units + per - 1) / per), moe::combine::kThreads, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(p, static_cast<int>(spw));
-  CUDA_TRY(cudaGetLastError(), "combine_kernel launch");
+  CUDA_TRY(launch_pdl(moe::combine::combine_kernel, dim3(static_cast<unsigned>((units + per - 1) / per)),
+                      dim3(moe::combine::kThreads), 0, static_cast<cudaStream_t>(stream), p, static_cast<int>(spw)),
+           "combine_kernel launch");
   return MOE_OK;
 }
 
@@ -794,9 +819,9 @@ int moe_quantize_int8(const void* w, int w_dtype, int64_t rows, int64_t K, int8_
   p.w_dtype = w_dtype;
   p.scale_bf16 = scale_dtype == MOE_DT_BF16;
   const int64_t per = moe::combine::kThreads / 32;
-  moe::combine::quantize_kernel<<<static_cast<unsigned>((rows + per - 1) / per), moe::combine::kThreads, 0,
-                                  static_cast<cudaStream_t>(stream)>>>(p);
-  CUDA_TRY(cudaGetLastError(), "quantize_kernel launch");
+  CUDA_TRY(launch_pdl(moe::combine::quantize_kernel, dim3(static_cast<unsigned>((rows + per - 1) / per)),
+                      dim3(moe::combine::kThreads), 0, static_cast<cudaStream_t>(stream), p),
+           "quantize_kernel launch");
   return MOE_OK;
 }
 
@@ -984,11 +1009,11 @@ int moe_ep_dispatch(const void* x, int x_dtype, int64_t T, int64_t H, const void
   const int64_t chunks = p.n > 0 ? (p.n + moe::ep::kChunk - 1) / moe::ep::kChunk : 1;
   unsigned split = 1;
   const int64_t per_row = H / 8;
-  while (split < 8 && chunks * split < 2 * sms && per_row % (2 * split) == 0 && per_row / (2 * split) >= 32)
+  while (split < 32 && chunks * split < 2 * sms && per_row % (2 * split) == 0 && per_row / (2 * split) >= 8)
     split *= 2;
-  moe::ep::dispatch_kernel<<<dim3(static_cast<unsigned>(chunks), split), moe::ep::kThreads, 0,
-                             static_cast<cudaStream_t>(stream)>>>(p);
-  CUDA_TRY(cudaGetLastError(), "dispatch_kernel launch");
+  CUDA_TRY(launch_pdl(moe::ep::dispatch_kernel, dim3(static_cast<unsigned>(chunks), split), dim3(moe::ep::kThreads),
+                      0, static_cast<cudaStream_t>(stream), p),
+           "dispatch_kernel launch");
   return MOE_OK;
 }
 

@@ -19,6 +19,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the previous kernel in its stream finishes:
+// pdl_trigger() lets the next kernel start its prologue early, and pdl_wait()
+// blocks until every prerequisite grid has completed and its writes are
+// visible. Each kernel here calls pdl_wait() before its first global memory
+// access, so the overlap covers only launch latency and set-up (barriers,
+// TMEM, descriptor prefetch). Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -18,6 +18,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxE = 256;
 constexpr int kMaxK = 16;
 constexpr int kMaxTB = 16;
+constexpr int kMaxSplits = 16;  // most f32 partial-logit slabs
 
 struct Params {
   const void* x;
@@ -91,6 +92,8 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
+  pdl_trigger();
+  pdl_wait();  // before the first global memory access
   extern __shared__ float smem_f[];
   const int tb = p.tb;
   const int E = p.E;
@@ -103,10 +106,16 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (p.logits_in) {
+    // all slab loads in flight first, then the sum in slab order
     const int64_t slab = p.T * E;
     for (int i = threadIdx.x; i < ntok * E; i += kThreads) {
-      float v = p.logits_in[t0 * E + i];
-      for (int s = 1; s < p.n_splits; ++s) v += p.logits_in[s * slab + t0 * E + i];
+      float part[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) part[s] = s < p.n_splits ? p.logits_in[s * slab + t0 * E + i] : 0.f;
+      float v = part[0];
+#pragma unroll
+      for (int s = 1; s < kMaxSplits; ++s)
+        if (s < p.n_splits) v += part[s];
       lg[i] = v;
     }
   } else {

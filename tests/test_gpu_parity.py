@@ -330,6 +330,23 @@ def test_layer_is_deterministic(c2_weights: LayerWeights) -> None:
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("t", [1, 16, 128])
+def test_captured_layer_replays_the_eager_bits(c2_weights: LayerWeights, t: int) -> None:
+    """The CUDA-graph decode step is the same kernels: same bits as the eager
+    call, for the captured input and for new inputs copied in."""
+    from dispatch_b200.kernels.layer import CapturedLayer
+
+    lw = c2_weights
+    g = torch.Generator(device="cuda").manual_seed(8)
+    ws, sh = StackedExpertWeights(lw.gate, lw.up, lw.down), SharedExpertWeights(*lw.shared)
+    cfg = RouterConfig(top_k=6)
+    cap = CapturedLayer(randn((t, 2048), g, 1.0), lw.router, ws, cfg, shared=sh)
+    for _ in range(3):
+        x = randn((t, 2048), g, 1.0)
+        got = cap(x).clone()
+        assert torch.equal(got, moe_layer_forward(x, lw.router, ws, cfg, shared=sh).out)
+
+
 def test_layer_prefill_4096_vs_torch_fp32(c2_weights: LayerWeights) -> None:
     """Full prefill size: checked against an f32 torch computation of the same
     math on the GPU (a floating-point reference, not the oracle)."""
