@@ -41,12 +41,19 @@ template <bool kInt8>
 struct Config {
   static constexpr int kStages = kInt8 ? 3 : 4;
   static constexpr uint32_t kStageBytes = A_BYTES + B_BYTES + (kInt8 ? Q_BYTES : 0);
-  // int8 build: six dequantiser warps (2-7) keep up with the MMA; the
-  // epilogue is always the last four warps (one per TMEM lane quarter).
-  static constexpr int kConvWarps = kInt8 ? 6 : 0;
+  // int8 build: eight dequantiser warps (2-9, two per SM sub-partition) keep
+  // up with the MMA; the epilogue is always the last four warps (one per TMEM
+  // lane quarter).
+  static constexpr int kConvWarps = kInt8 ? 8 : 0;
   static constexpr int kConvThreads = 32 * kConvWarps;
+  // 16-byte int8 chunks per dequantiser thread and stage (a 256-row tile)
+  static constexpr int kConvItems = kInt8 ? (BN * (BK / 16) + kConvThreads - 1) / kConvThreads : 0;
   static constexpr int kEpiWarp0 = 2 + kConvWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + 4);
+  // Each SM sub-partition holds a quarter of the 64K registers and the
+  // CTA's warps are spread over the four: the busiest one holds
+  // ceil(warps / 4) warps.
+  static constexpr int kMaxRegs = (16384 / (32 * ((kThreads / 32 + 3) / 4))) & ~7;
 };
 
 struct Segment {
@@ -152,6 +159,30 @@ __device__ __forceinline__ float ld_scale(const void* p, int bf16, int64_t i) {
   return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
 }
 
+// Eight consecutive per-channel scales from index i (n valid, the rest 1):
+// one or two 16-byte loads when aligned, else scalar loads.
+__device__ __forceinline__ void ld_scales8(const void* p, int bf16, int64_t i, int n, float (&s)[8]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p) + static_cast<uintptr_t>(i) * (bf16 ? 2u : 4u);
+  if (n >= 8 && (a & 15u) == 0) {
+    if (bf16) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(a));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[2 * j] = __uint_as_float(w[j] << 16);
+        s[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    } else {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(a));
+      const float4 y = __ldg(reinterpret_cast<const float4*>(a) + 1);
+      s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w; s[4] = y.x; s[5] = y.y; s[6] = y.z; s[7] = y.w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = j < n ? ld_scale(p, bf16, i + j) : 1.f;
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, int f16) {
   if (f16) {
     __half2 h = __floats2half2_rn(a, b);
@@ -244,7 +275,8 @@ __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi
 }
 
 template <bool kInt8>
-__global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(Config<kInt8>::kThreads)
+    __maxnreg__(Config<kInt8>::kMaxRegs < 168 ? Config<kInt8>::kMaxRegs : 168) grouped_gemm_kernel(const __grid_constant__ Params p) {
   using Cfg = Config<kInt8>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -460,14 +492,25 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
             if (!wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status)) { ok = false; break; }
             const uint8_t* q = sQ + stage * Q_BYTES;
             uint8_t* b = sB + stage * B_BYTES;
-            for (int item = ct; item < items; item += Cfg::kConvThreads) {
-              const int r = item >> 2, cc = item & 3;
-              const uint4 v = *reinterpret_cast<const uint4*>(q + r * 64 + cc * 16);
-              uint4 lo, hi;
-              dequant16(v, p.in_f16, lo, hi);
-              uint8_t* row = b + r * 128;
-              *reinterpret_cast<uint4*>(row + (((2 * cc) ^ (r & 7)) << 4)) = lo;
-              *reinterpret_cast<uint4*>(row + (((2 * cc + 1) ^ (r & 7)) << 4)) = hi;
+            // all of this thread's chunk loads first, then dequantise and store
+            constexpr int NI = Cfg::kConvItems;
+            uint4 v[NI];
+#pragma unroll
+            for (int j = 0; j < NI; ++j) {
+              const int item = ct + j * Cfg::kConvThreads;
+              if (item < items) v[j] = *reinterpret_cast<const uint4*>(q + (item >> 2) * 64 + (item & 3) * 16);
+            }
+#pragma unroll
+            for (int j = 0; j < NI; ++j) {
+              const int item = ct + j * Cfg::kConvThreads;
+              if (item < items) {
+                const int r = item >> 2, cc = item & 3;
+                uint4 lo, hi;
+                dequant16(v[j], p.in_f16, lo, hi);
+                uint8_t* row = b + r * 128;
+                *reinterpret_cast<uint4*>(row + (((2 * cc) ^ (r & 7)) << 4)) = lo;
+                *reinterpret_cast<uint4*>(row + (((2 * cc + 1) ^ (r & 7)) << 4)) = hi;
+              }
             }
             fence_proxy_async_smem();
             mbar_arrive(&c.conv[stage]);
@@ -530,14 +573,23 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
             const int nc = min(32, Sg.n - col0);
             float h[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float g = __uint_as_float(gv[j]);
-              float u = __uint_as_float(uv[j]);
-              if (kInt8 && Sg.b_int8 && j < nc) {
-                g *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
-                u *= ld_scale(Sg.scale1, Sg.scale_bf16, sc_base + col0 + j);
+            for (int q8 = 0; q8 < 4; ++q8) {
+              float gs[8], us[8];
+              if (kInt8 && Sg.b_int8) {
+                ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, gs);
+                ld_scales8(Sg.scale1, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, us);
               }
-              h[j] = g / (1.0f + __expf(-g)) * u;
+#pragma unroll
+              for (int j8 = 0; j8 < 8; ++j8) {
+                const int j = 8 * q8 + j8;
+                float g = __uint_as_float(gv[j]);
+                float u = __uint_as_float(uv[j]);
+                if (kInt8 && Sg.b_int8 && j < nc) {
+                  g *= gs[j8];
+                  u *= us[j8];
+                }
+                h[j] = g / (1.0f + __expf(-g)) * u;
+              }
             }
             if (staged)
               store_block32_staged(estage, h, p.in_f16, lane, rowp, col0);
@@ -556,9 +608,15 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads, 1) grouped_gemm_kerne
             const int nc = min(32, Sg.n - col0);
             float o[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              o[j] = __uint_as_float(v[j]);
-              if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + col0 + j);
+            for (int q8 = 0; q8 < 4; ++q8) {
+              float ss[8];
+              if (kInt8 && Sg.b_int8) ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, ss);
+#pragma unroll
+              for (int j8 = 0; j8 < 8; ++j8) {
+                const int j = 8 * q8 + j8;
+                o[j] = __uint_as_float(v[j]);
+                if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ss[j8];
+              }
             }
             if (staged)
               store_block32_staged(estage, o, p.in_f16, lane, rowp, col0);
