@@ -336,7 +336,7 @@ def run_b200(args, wl: Workload) -> None:
     import torch
 
     from dispatch_b200 import _lib as L
-    from dispatch_b200.kernels.layer import CapturedLayer, RouterConfig, moe_layer_forward
+    from dispatch_b200.kernels.layer import CapturedLayer, RouterConfig, moe_layer_forward, run_host_batches
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -352,6 +352,17 @@ def run_b200(args, wl: Workload) -> None:
         bias = (-1.2 * torch.log(torch.arange(wl.E, dtype=torch.float32, device=dev) + 1.0))
 
     ep = None
+    if args.profile_calls:
+        # profiler driver: the bare layer call, no timing and no JSON line
+        if world > 1:
+            raise SystemExit("--profile-calls runs on one GPU (profile one process, never a multi-rank job)")
+        for _ in range(args.profile_calls):
+            moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)
+        torch.cuda.synchronize()
+        L.check_device_status(dev)
+        print(f"profile-calls ok: {args.profile_calls} x {wl.name} T={t}", flush=True)
+        return
+
     if world > 1:
         if args.ep_transport == "peer":
             from dispatch_b200.kernels.ep_peer import PeerEPLayer
@@ -384,16 +395,15 @@ def run_b200(args, wl: Workload) -> None:
     L.check_device_status(dev)
     value = t * world / (ms * 1e-3)
 
-    # e2e: the public call with host buffers (pinned), copies inside the timed region
+    # e2e: the public host-batch call (run_host_batches) on pinned host buffers;
+    # every step's host->device input copy and device->host output copy are in
+    # the timed region, on copy streams that overlap the neighbouring steps
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(t, wl.H, dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty_like(x)
-
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        out_host.copy_(layer(x_dev), non_blocking=True)
-
-    e2e_ms = max_over_ranks(time_loop(e2e_step, max(args.steps // 2, 3), 3, world, stream), world)
+    n_e2e = max(args.steps // 2, 3)
+    e2e_ms = max_over_ranks(
+        time_loop(lambda: run_host_batches(layer, [x_host] * n_e2e, [out_host] * n_e2e), 1, 1, world, stream),
+        world) / n_e2e
     e2e_val = t * world / (e2e_ms * 1e-3)
 
     # dominant kernel: the gate/up tcgen05 GEMM (+SwiGLU epilogue), timed alone
@@ -521,6 +531,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: NVLink peer stores fused into dispatch/FFN (peer) or NCCL all-to-all (nccl)")
+    ap.add_argument("--profile-calls", type=int, default=0,
+                    help="run the layer this many times and exit (a driver for ncu launch lists and captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -196,3 +196,43 @@ class CapturedLayer:
         self.x.copy_(x)
         self.graph.replay()
         return self.result.out
+
+
+def run_host_batches(fn, inputs: list[torch.Tensor], outputs: list[torch.Tensor]) -> None:
+    """``outputs[i][:] = fn(inputs[i])`` for host (pinned) batches, with the
+    copies off the compute stream: batch i+1's host->device copy and batch
+    i-1's device->host copy run on their own streams while ``fn`` computes
+    batch i, so a stream of requests costs max(copy, compute) per batch
+    instead of their sum. ``fn`` is any layer call (``moe_layer_forward(...).out``,
+    a ``CapturedLayer``, an expert-parallel layer) that runs on the current
+    stream. Returns with all work enqueued and the current stream ordered after
+    the last copy; synchronise before reading ``outputs``."""
+    if not inputs:
+        return
+    if len(inputs) != len(outputs):
+        raise ValueError(f"{len(inputs)} inputs but {len(outputs)} outputs")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    comp = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    slots = [torch.empty(inputs[0].shape, dtype=inputs[0].dtype, device=dev) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for i, (xin, yout) in enumerate(zip(inputs, outputs)):
+        s = i % 2
+        if xin.shape != slots[s].shape or xin.dtype != slots[s].dtype:
+            raise ValueError("all input batches must share one shape and dtype")
+        with torch.cuda.stream(h2d):
+            if i >= 2:
+                h2d.wait_event(free[s])  # the layer has finished reading this slot
+            slots[s].copy_(xin, non_blocking=True)
+            ready[s].record(h2d)
+        comp.wait_event(ready[s])
+        out = fn(slots[s])
+        free[s].record(comp)
+        d2h.wait_stream(comp)
+        with torch.cuda.stream(d2h):
+            yout.copy_(out, non_blocking=True)
+        out.record_stream(d2h)
+    comp.wait_stream(d2h)
+    for t in slots:
+        t.record_stream(h2d)

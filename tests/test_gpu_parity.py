@@ -347,6 +347,23 @@ def test_captured_layer_replays_the_eager_bits(c2_weights: LayerWeights, t: int)
         assert torch.equal(got, moe_layer_forward(x, lw.router, ws, cfg, shared=sh).out)
 
 
+def test_host_batches_overlap_copies_and_keep_the_bits(c2_weights: LayerWeights) -> None:
+    """run_host_batches: each host batch's output is the eager layer's output."""
+    from dispatch_b200.kernels.layer import run_host_batches
+
+    lw = c2_weights
+    g = torch.Generator(device="cuda").manual_seed(9)
+    ws, sh = StackedExpertWeights(lw.gate, lw.up, lw.down), SharedExpertWeights(*lw.shared)
+    cfg = RouterConfig(top_k=6)
+    xs = [randn((96, 2048), g, 1.0) for _ in range(5)]
+    ins = [x.cpu().pin_memory() for x in xs]
+    outs = [torch.empty(96, 2048, dtype=torch.bfloat16).pin_memory() for _ in xs]
+    run_host_batches(lambda x: moe_layer_forward(x, lw.router, ws, cfg, shared=sh).out, ins, outs)
+    torch.cuda.synchronize()
+    for x, o in zip(xs, outs):
+        assert torch.equal(o, moe_layer_forward(x, lw.router, ws, cfg, shared=sh).out.cpu())
+
+
 def test_layer_prefill_4096_vs_torch_fp32(c2_weights: LayerWeights) -> None:
     """Full prefill size: checked against an f32 torch computation of the same
     math on the GPU (a floating-point reference, not the oracle)."""
