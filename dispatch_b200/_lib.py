@@ -115,9 +115,13 @@ _SIGNATURES = {
          _i64, _p, _p, _p, _p, _p, _sz, _p, _p],
         _i32,
     ),
+    "moe_ep_signal_bytes": ([_i32, _i64], _sz),
+    "moe_ep_exchange": ([_p, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _p], _i32),
 }
 
 PEER_HANDLE_BYTES = 64
+EP_SIGNAL_HEADER_BYTES = 256
+EP_FLAG_SLOTS = 4
 EP_MAX_RANKS = 16
 
 _lib: ctypes.CDLL | None = None

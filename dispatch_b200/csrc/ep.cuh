@@ -151,5 +151,58 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(const DispatchParams
   __threadfence_system();
 }
 
+// ---------------------------------------------------------------------------
+// Exchange / barrier over the ranks' signal buffers (one CTA). Signal buffer
+// layout: int32 flags[kFlagSlots][kMaxRanks] in the first kSignalHeader bytes,
+// then an int32 payload area of (world, n).
+constexpr int kFlagSlots = 4;
+constexpr int kSignalHeader = 256;
+static_assert(kFlagSlots * kMaxRanks * 4 <= kSignalHeader, "flag rows fit the header");
+
+struct ExchangeParams {
+  const int32_t* payload;  // n int32 of this rank (may be null when n == 0)
+  int64_t n;
+  void* const* peer_signal;  // (world) signal buffers as mapped here (own entry = local)
+  int32_t* local_signal;
+  int slot, rank, world;
+  int32_t epoch;
+  int32_t* status;
+};
+
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) exchange_kernel(const ExchangeParams p) {
+  pdl_trigger();
+  pdl_wait();  // the previous kernel's stores (payload, peer rows) are complete
+  const int tid = threadIdx.x;
+  for (int d = 0; d < p.world; ++d) {
+    int32_t* dst = reinterpret_cast<int32_t*>(static_cast<char*>(p.peer_signal[d]) + kSignalHeader) + p.rank * p.n;
+    for (int64_t i = tid; i < p.n; i += blockDim.x) dst[i] = p.payload[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < p.world) {
+    st_release_sys(static_cast<int32_t*>(p.peer_signal[tid]) + p.slot * kMaxRanks + p.rank, p.epoch);
+    const int32_t* f = p.local_signal + p.slot * kMaxRanks + tid;
+    const uint64_t t0 = globaltimer_ns();
+    // wrap-safe "flag < epoch" on the int32 epoch sequence
+    while (static_cast<int32_t>(static_cast<uint32_t>(ld_acquire_sys(f)) - static_cast<uint32_t>(p.epoch)) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (p.status) atomicCAS(p.status, 0, MOE_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 }  // namespace ep
 }  // namespace moe

@@ -1036,4 +1036,38 @@ int moe_ep_expert_ffn(const void* recv, int act_dtype, int64_t recv_cap, int64_t
                   shared_up, shared_down, nullptr, y_shared, workspace, workspace_bytes, status, stream, ro);
 }
 
+
+static_assert(MOE_EP_SIGNAL_HEADER_BYTES == moe::ep::kSignalHeader && MOE_EP_FLAG_SLOTS == moe::ep::kFlagSlots,
+              "signal buffer layout");
+
+size_t moe_ep_signal_bytes(int world, int64_t n) {
+  if (world < 1 || n < 0) return 0;
+  return MOE_EP_SIGNAL_HEADER_BYTES + static_cast<size_t>(world) * static_cast<size_t>(n) * sizeof(int32_t);
+}
+
+int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal, int slot,
+                    int rank, int world, int32_t epoch, int32_t* status, void* stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  CHECK_ARG(world >= 1 && world <= MOE_EP_MAX_RANKS && rank >= 0 && rank < world, "rank %d / world %d out of range",
+            rank, world);
+  CHECK_ARG(slot >= 0 && slot < MOE_EP_FLAG_SLOTS, "flag slot %d not in [0, %d)", slot, MOE_EP_FLAG_SLOTS);
+  CHECK_ARG(n >= 0 && (n == 0 || payload), "payload of %lld int32 needs a pointer", (long long)n);
+  CHECK_ARG(peer_signal && local_signal, "null signal buffer");
+  moe::ep::ExchangeParams p;
+  p.payload = payload;
+  p.n = n;
+  p.peer_signal = peer_signal;
+  p.local_signal = local_signal;
+  p.slot = slot;
+  p.rank = rank;
+  p.world = world;
+  p.epoch = epoch;
+  p.status = status;
+  CUDA_TRY(launch_pdl(moe::ep::exchange_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), p),
+           "exchange_kernel launch");
+  return MOE_OK;
+}
+
 }  // extern "C"

@@ -6,11 +6,12 @@ include/moe_ep_b200.h).
 One ``PeerEPLayer`` call on a rank's T local tokens:
 
 1. route and group locally (stable counting sort; no row copy);
-2. NCCL all-gather of the (E,) per-expert counts -> the (world, E) matrix,
-   which fixes every rank's receive layout on every rank;
+2. all-gather of the (E,) per-expert counts -> the (world, E) matrix, which
+   fixes every rank's receive layout on every rank (``moe_ep_exchange``: one
+   CTA stores the counts into every peer's signal buffer and exchanges flags);
 3. ``moe_ep_dispatch``: each (token, slot) row is stored by this GPU straight
    into the receive buffer of the expert's owner, with its return code;
-4. barrier (a 1-element NCCL all-reduce, stream-ordered);
+4. barrier (``moe_ep_exchange`` with no payload, stream-ordered);
 5. ``moe_ep_expert_ffn``: the grouped SwiGLU FFN over the received rows (and
    the shared expert over the local tokens, in the same two launches); the
    down projection's epilogue stores each output row straight into the
@@ -67,8 +68,10 @@ class PeerBuffers:
             bad = [int(d) for d in devs.tolist() if not lib.moe_peer_can_access(int(d))]
             if bad:
                 raise RuntimeError(f"rank {rank} (cuda:{dev.index}) cannot map the memory of devices {bad}")
-            sizes = (self.recv_cap * hidden * 2, self.recv_cap * 4, self.back_rows * hidden * 2)
-            handles = (ctypes.c_uint8 * (3 * L.PEER_HANDLE_BYTES))()
+            sizes = (self.recv_cap * hidden * 2, self.recv_cap * 4, self.back_rows * hidden * 2,
+                     lib.moe_ep_signal_bytes(world, n_experts))
+            nb = len(sizes)
+            handles = (ctypes.c_uint8 * (nb * L.PEER_HANDLE_BYTES))()
             for i, n in enumerate(sizes):
                 p = ctypes.c_void_p()
                 L.check(lib.moe_peer_alloc(n, ctypes.byref(p)), "moe_peer_alloc")
@@ -78,10 +81,10 @@ class PeerBuffers:
             local = torch.frombuffer(bytearray(handles), dtype=torch.uint8).to(dev)
             allh = torch.empty(world * local.numel(), dtype=torch.uint8, device=dev)
             dist.all_gather_into_tensor(allh, local, group=group)
-            allh = allh.view(world, 3, L.PEER_HANDLE_BYTES).cpu()
-            table = [[0] * world for _ in range(3)]
+            allh = allh.view(world, nb, L.PEER_HANDLE_BYTES).cpu()
+            table = [[0] * world for _ in range(nb)]
             for s in range(world):
-                for i in range(3):
+                for i in range(nb):
                     if s == rank:
                         table[i][s] = self._own[i]
                         continue
@@ -90,20 +93,34 @@ class PeerBuffers:
                     L.check(lib.moe_peer_import(raw, ctypes.byref(p)), "moe_peer_import")
                     self._mapped.append(p.value)
                     table[i][s] = p.value
-            self.recv_ptr, self.ret_ptr, self.back_ptr = self._own
+            self.recv_ptr, self.ret_ptr, self.back_ptr, self.signal_ptr = self._own
             self.t_recv = torch.tensor(table[0], dtype=torch.int64, device=dev)
             self.t_ret = torch.tensor(table[1], dtype=torch.int64, device=dev)
             self.t_back = torch.tensor(table[2], dtype=torch.int64, device=dev)
-            self.counts_all = torch.zeros(world * n_experts, dtype=torch.int32, device=dev)
+            self.t_signal = torch.tensor(table[3], dtype=torch.int64, device=dev)
+            # the (world, E) count matrix lives in the signal buffer's payload area
+            self.counts_all_ptr = self.signal_ptr + L.EP_SIGNAL_HEADER_BYTES
+            self.epoch = 0
             self.recv_offsets = torch.zeros(self.e_loc + 1, dtype=torch.int32, device=dev)
             self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
             self.barrier()
             torch.cuda.synchronize(dev)
 
     def barrier(self) -> None:
-        """Stream-ordered barrier over the group: kernels enqueued after it on
-        any rank run after every rank's kernels enqueued before it."""
+        """Stream-ordered barrier over the group (NCCL): kernels enqueued after
+        it on any rank run after every rank's kernels enqueued before it."""
         dist.all_reduce(self._flag, group=self.group)
+
+    def exchange(self, payload: torch.Tensor | None, slot: int, epoch: int) -> None:
+        """``moe_ep_exchange``: ``payload`` (int32, or None) into row ``rank`` of
+        every rank's count area, then a flag barrier on ``slot`` for ``epoch``."""
+        dev = self.device
+        n = 0 if payload is None else payload.numel()
+        epoch = ((epoch + 2**31) % 2**32) - 2**31  # the kernel compares int32 epochs wrap-safely
+        rc = self._lib.moe_ep_exchange(
+            None if payload is None else payload.data_ptr(), n, self.t_signal.data_ptr(), self.signal_ptr, slot,
+            self.rank, self.world, epoch, L.status_word(dev).data_ptr(), L.stream_ptr(dev))
+        L.check(rc, "moe_ep_exchange")
 
     def close(self) -> None:
         """Collective: unmaps the peers' buffers and frees this rank's."""
@@ -158,8 +175,8 @@ class PeerEPLayer:
         self.buf = buffers or PeerBuffers(rank=rank, world=world, group=group, device=g.device,
                                           max_tokens=max_tokens, top_k=self.top_k, hidden=self.hidden,
                                           n_experts=e, act_dtype=self.act_dtype)
-        # launches of this library per call: route x2, group x2, dispatch, FFN x2, combine
-        self.launches_per_step = 8
+        # launches of this library per call: route x2, group x2, exchange x3, dispatch, FFN x2, combine
+        self.launches_per_step = 11
 
     def close(self) -> None:
         if self._own_buffers:
@@ -184,14 +201,16 @@ class PeerEPLayer:
         k = self.top_k
         idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
         counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
-        dist.all_gather_into_tensor(buf.counts_all, counts, group=self.group)
+        buf.epoch += 1
+        epoch = buf.epoch
+        buf.exchange(counts, 0, epoch)
         rc = lib.moe_ep_dispatch(
             x.data_ptr(), L.dt(x), t, h, idx.data_ptr(), L.dt(idx), k, pos.data_ptr(), offsets.data_ptr(),
-            buf.counts_all.data_ptr(), self.rank, self.world, self.n_experts, buf.t_recv.data_ptr(),
+            buf.counts_all_ptr, self.rank, self.world, self.n_experts, buf.t_recv.data_ptr(),
             buf.t_ret.data_ptr(), buf.recv_cap, buf.recv_offsets.data_ptr(), st, stream,
         )
         L.check(rc, "moe_ep_dispatch")
-        buf.barrier()
+        buf.exchange(None, 1, epoch)
         sh = self.shared
         i_sh = 0 if sh is None else sh.gate.shape[0]
         ys = torch.empty(t, h, dtype=x.dtype, device=dev) if sh is not None else None
@@ -210,7 +229,7 @@ class PeerEPLayer:
             L.ptr(None if sh is None else sh.down), L.ptr(ys), ws.data_ptr(), ws.numel(), st, stream,
         )
         L.check(rc, "moe_ep_expert_ffn")
-        buf.barrier()
+        buf.exchange(None, 2, epoch)
         out = torch.empty(t, h, dtype=x.dtype, device=dev)
         rc = lib.moe_combine(buf.back_ptr, L.dt(x), pos.data_ptr(), wf.data_ptr(), t, k, h, L.ptr(ys),
                              out.data_ptr(), L.dt(out), st, stream)

@@ -110,6 +110,30 @@ int moe_ep_expert_ffn(const void* recv, int act_dtype, int64_t recv_cap, int64_t
                       const void* shared_up, const void* shared_down, void* y_shared, void* workspace,
                       size_t workspace_bytes, int32_t* status, void* stream);
 
+/*
+ * Stream-ordered exchange and barrier over the ranks' signal buffers, in
+ * place of the NCCL all-gather and barriers around the dispatch and the FFN
+ * (the synchronisation DeepEP's Buffer does inside dispatch/combine,
+ * src/dispatch/kernels/expert_parallel.py:160-187).
+ *
+ * A signal buffer (moe_ep_signal_bytes, from moe_peer_alloc, zero at
+ * allocation) holds MOE_EP_FLAG_SLOTS rows of MOE_EP_MAX_RANKS int32 flags
+ * in its first MOE_EP_SIGNAL_HEADER_BYTES, then a (world, n) int32 payload
+ * area. One launch (a single CTA) on this rank: copies `payload` (n int32, may
+ * be 0) into row `rank` of every rank's payload area, fences at system scope,
+ * stores `epoch` into flag [slot][rank] of every rank (release), then waits
+ * until flags [slot][0..world) of its own buffer are >= epoch (acquire).
+ * Kernels enqueued after it see every rank's stores made before that rank's
+ * exchange. Every rank makes the same calls with the same epoch, which grows
+ * by one per layer call. The wait is bounded (2 s): on expiry it sets
+ * MOE_ERR_TIMEOUT in the status word and returns.
+ */
+#define MOE_EP_SIGNAL_HEADER_BYTES 256
+#define MOE_EP_FLAG_SLOTS 4
+size_t moe_ep_signal_bytes(int world, int64_t n);
+int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal, int slot,
+                    int rank, int world, int32_t epoch, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
