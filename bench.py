@@ -376,7 +376,7 @@ def run_b200(args, wl: Workload) -> None:
         def layer(xx):
             return ep(xx)
 
-        launches_per_step = ep.launches_per_step
+        launches_per_step = ep.launches_for(t) if hasattr(ep, "launches_for") else ep.launches_per_step
         parallelism = f"ep{world} ({args.ep_transport})"
     else:
         def layer(xx):
