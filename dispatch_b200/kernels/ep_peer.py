@@ -153,7 +153,7 @@ class PeerEPLayer:
     def __init__(self, router_weight, weights, shared, router_cfg, *, rank: int, world: int, group=None,
                  e_score_bias=None, n_experts: int | None = None, weights_are_local: bool = False,
                  max_tokens: int = 4096, act_dtype: torch.dtype = torch.bfloat16,
-                 buffers: PeerBuffers | None = None, overlap_shared: bool = True,
+                 buffers: PeerBuffers | None = None, overlap_shared: bool = False,
                  overlap_min_tokens: int = 1024):
         from dispatch_b200.kernels.expert_parallel import _slice_experts  # noqa: PLC0415
         from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights  # noqa: PLC0415
@@ -181,7 +181,9 @@ class PeerEPLayer:
         # leave room on each SM for the small dispatch and exchange kernels).
         # Measured at 2 GPUs: 0.720 -> 0.711 ms at 4096 tokens, but 0.204 ->
         # 0.239 ms at 128 (two more launches and a stream join), so only calls
-        # of at least overlap_min_tokens tokens split it off.
+        # of at least overlap_min_tokens tokens split it off. Off by default:
+        # at 8 GPUs the step was slower with it (0.92 ms), the shared GEMM's
+        # persistent CTAs leaving one dispatch CTA per SM for 7x more rows.
         self.overlap_shared = overlap_shared and shared is not None
         self.overlap_min_tokens = overlap_min_tokens
         self._side: torch.cuda.Stream | None = None
