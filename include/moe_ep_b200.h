@@ -19,9 +19,10 @@
  *
  * No row is staged through a send buffer and nothing is synchronised with the
  * host: the only collectives are an all-gather of the (E,) per-expert counts
- * and two stream-ordered barriers, which the caller issues (NCCL). Peer
- * memory is plain CUDA IPC (cudaIpcGetMemHandle / cudaIpcOpenMemHandle): no
- * multicast object, no TMA multicast load.
+ * and two stream-ordered barriers, each one moe_ep_exchange launch over the
+ * ranks' signal buffers (an NCCL all-gather and all-reduce serve as well).
+ * Peer memory is plain CUDA IPC (cudaIpcGetMemHandle / cudaIpcOpenMemHandle):
+ * no multicast object, no TMA multicast load.
  *
  * Receive layout on the rank that owns experts [rank*E_loc, (rank+1)*E_loc):
  * local expert j's rows are contiguous, j-major; inside a block the rows come
