@@ -21,6 +21,8 @@ namespace group {
 constexpr int kThreads = 256;
 constexpr int kChunk = kThreads;
 constexpr int kMaxE = 256;
+constexpr int kHistTile = 8192;  // int32 histogram entries staged per block (32 KiB)
+static_assert(kMaxE <= kThreads, "one thread per expert in the scatter's base sums");
 
 struct Params {
   const void* idx;
@@ -106,18 +108,34 @@ __global__ void __launch_bounds__(kThreads) group_scatter_kernel(const Params p)
   __shared__ int wcnt[kThreads / 32][kMaxE];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
-  // per expert: rows in earlier chunks and rows overall
-  for (int e = tid; e < p.E; e += kThreads) {
-    int before = 0, all = 0;
-    for (int cc = 0; cc < p.nchunks; ++cc) {
-      const int v = p.hist[static_cast<int64_t>(cc) * p.E + e];
-      before += cc < c ? v : 0;
-      all += v;
+  // per expert: rows in earlier chunks and rows overall. The (nchunks, E)
+  // histograms are staged through shared memory a block of chunks at a time
+  // (every thread's loads of a block are independent and in flight together);
+  // a per-thread serial walk over global memory was a long chain of L2
+  // round trips at prefill sizes.
+  __shared__ int tile[kHistTile];
+  const int rows_per_tile = kHistTile / p.E;
+  int before = 0, all = 0;  // for expert tid (tid < E; E <= kThreads)
+  for (int cc0 = 0; cc0 < p.nchunks; cc0 += rows_per_tile) {
+    const int rows = min(rows_per_tile, p.nchunks - cc0);
+    const int n_items = rows * p.E;
+    const int* src = p.hist + static_cast<int64_t>(cc0) * p.E;
+    for (int i = tid; i < n_items; i += kThreads) tile[i] = src[i];
+    __syncthreads();
+    if (tid < p.E) {
+      for (int j = 0; j < rows; ++j) {
+        const int v = tile[j * p.E + tid];
+        before += cc0 + j < c ? v : 0;
+        all += v;
+      }
     }
-    base[e] = before;
-    total[e] = all;
+    __syncthreads();
+  }
+  if (tid < p.E) {
+    base[tid] = before;
+    total[tid] = all;
 #pragma unroll
-    for (int w = 0; w < kThreads / 32; ++w) wcnt[w][e] = 0;
+    for (int w = 0; w < kThreads / 32; ++w) wcnt[w][tid] = 0;
   }
   __syncthreads();
   // exclusive prefix sum over experts (one warp), added to the chunk bases
