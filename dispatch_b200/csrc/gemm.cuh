@@ -41,10 +41,11 @@ template <bool kInt8>
 struct Config {
   static constexpr int kStages = kInt8 ? 3 : 4;
   static constexpr uint32_t kStageBytes = A_BYTES + B_BYTES + (kInt8 ? Q_BYTES : 0);
-  // int8 build: eight dequantiser warps (2-9, two per SM sub-partition) keep
-  // up with the MMA; the epilogue is always the last four warps (one per TMEM
-  // lane quarter).
-  static constexpr int kConvWarps = kInt8 ? 8 : 0;
+  // int8 build: ten dequantiser warps (2-11; 16 warps in all, four per SM
+  // sub-partition, the most that 128 registers a thread allow); the epilogue
+  // is always the last four warps (one per TMEM lane quarter). Same box, C3
+  // T=4096: 6 warps 1.18 ms, 8 warps 0.908 ms, 10 warps 0.896 ms.
+  static constexpr int kConvWarps = kInt8 ? 10 : 0;
   static constexpr int kConvThreads = 32 * kConvWarps;
   // 16-byte int8 chunks per dequantiser thread and stage (a 256-row tile)
   static constexpr int kConvItems = kInt8 ? (BN * (BK / 16) + kConvThreads - 1) / kConvThreads : 0;
