@@ -223,3 +223,43 @@ def test_assign_experts_to_ranks_mirror() -> None:
         assign_experts_to_ranks(1, 2)
     with pytest.raises(ValueError, match="positive"):
         assign_experts_to_ranks(0, 2)
+
+
+def test_peer_buffers_refuse_bad_shapes_before_touching_a_device() -> None:
+    from dispatch_b200.kernels.ep_peer import PeerBuffers
+
+    common = dict(rank=0, device=torch.device("cuda", 0), max_tokens=8, top_k=2, hidden=64)
+    with pytest.raises(ValueError, match="world"):
+        PeerBuffers(world=17, n_experts=34, **common)
+    with pytest.raises(ValueError, match="split evenly"):
+        PeerBuffers(world=3, n_experts=8, **common)
+    with pytest.raises(ValueError, match="16-bit"):
+        PeerBuffers(world=2, n_experts=8, act_dtype=torch.float32, **common)
+
+
+def test_signal_buffer_size_is_host_arithmetic() -> None:
+    from dispatch_b200 import _lib as L
+
+    lib = L.lib()
+    assert lib.moe_ep_signal_bytes(8, 64) == L.EP_SIGNAL_HEADER_BYTES + 8 * 64 * 4
+    assert lib.moe_ep_signal_bytes(1, 0) == L.EP_SIGNAL_HEADER_BYTES
+    assert lib.moe_ep_signal_bytes(0, 64) == 0
+    # 4 slots x 16 rank flags of int32 fit the header
+    assert L.EP_FLAG_SLOTS * L.EP_MAX_RANKS * 4 <= L.EP_SIGNAL_HEADER_BYTES
+
+
+def test_exchange_without_a_device_reports_it() -> None:
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from dispatch_b200 import _lib as L
+
+    rc = L.lib().moe_ep_exchange(None, 0, None, None, 0, 0, 1, 1, None, None)
+    assert rc == L.MOE_ERR_NO_DEVICE
+
+
+def test_host_batches_check_lengths_before_any_copy() -> None:
+    from dispatch_b200.kernels.layer import run_host_batches
+
+    run_host_batches(lambda x: x, [], [])  # nothing to do
+    with pytest.raises(ValueError, match="outputs"):
+        run_host_batches(lambda x: x, [torch.zeros(2, 8)], [])
