@@ -205,8 +205,12 @@ def run_host_batches(fn, inputs: list[torch.Tensor], outputs: list[torch.Tensor]
     batch i, so a stream of requests costs max(copy, compute) per batch
     instead of their sum. ``fn`` is any layer call (``moe_layer_forward(...).out``,
     a ``CapturedLayer``, an expert-parallel layer) that runs on the current
-    stream. Returns with all work enqueued and the current stream ordered after
-    the last copy; synchronise before reading ``outputs``."""
+    stream; it may return a fresh tensor or the same buffer every call (a
+    ``CapturedLayer`` does): each result is copied on the compute stream into
+    one of two private device buffers, which the device->host copy reads, so
+    the next batch never overwrites a result still being copied out. Returns
+    with all work enqueued and the current stream ordered after the last copy;
+    synchronise before reading ``outputs``."""
     if not inputs:
         return
     if len(inputs) != len(outputs):
@@ -217,6 +221,8 @@ def run_host_batches(fn, inputs: list[torch.Tensor], outputs: list[torch.Tensor]
     slots = [torch.empty(inputs[0].shape, dtype=inputs[0].dtype, device=dev) for _ in range(2)]
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
+    snaps: list[torch.Tensor | None] = [None, None]  # private copies of the results
+    copied = [torch.cuda.Event() for _ in range(2)]  # device->host copy of a snapshot done
     for i, (xin, yout) in enumerate(zip(inputs, outputs)):
         s = i % 2
         if xin.shape != slots[s].shape or xin.dtype != slots[s].dtype:
@@ -229,10 +235,20 @@ def run_host_batches(fn, inputs: list[torch.Tensor], outputs: list[torch.Tensor]
         comp.wait_event(ready[s])
         out = fn(slots[s])
         free[s].record(comp)
+        if snaps[s] is None:
+            snaps[s] = torch.empty(out.shape, dtype=out.dtype, device=dev)
+        elif snaps[s].shape != out.shape or snaps[s].dtype != out.dtype:
+            raise ValueError("fn must return one shape and dtype for every batch")
+        else:
+            comp.wait_event(copied[s])  # batch i-2's result has left this snapshot
+        snaps[s].copy_(out)
         d2h.wait_stream(comp)
         with torch.cuda.stream(d2h):
-            yout.copy_(out, non_blocking=True)
-        out.record_stream(d2h)
+            yout.copy_(snaps[s], non_blocking=True)
+            copied[s].record(d2h)
     comp.wait_stream(d2h)
     for t in slots:
         t.record_stream(h2d)
+    for t in snaps:
+        if t is not None:
+            t.record_stream(d2h)

@@ -362,6 +362,15 @@ def test_host_batches_overlap_copies_and_keep_the_bits(c2_weights: LayerWeights)
     torch.cuda.synchronize()
     for x, o in zip(xs, outs):
         assert torch.equal(o, moe_layer_forward(x, lw.router, ws, cfg, shared=sh).out.cpu())
+    # a CUDA-graph layer returns the same output buffer every call
+    from dispatch_b200.kernels.layer import CapturedLayer
+
+    cap = CapturedLayer(xs[0], lw.router, ws, cfg, shared=sh)
+    outs2 = [torch.empty(96, 2048, dtype=torch.bfloat16).pin_memory() for _ in xs]
+    run_host_batches(cap, ins, outs2)
+    torch.cuda.synchronize()
+    for o, o2 in zip(outs, outs2):
+        assert torch.equal(o, o2)
 
 
 def test_layer_prefill_4096_vs_torch_fp32(c2_weights: LayerWeights) -> None:
