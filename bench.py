@@ -7,8 +7,12 @@ DeepSeek-V2-Lite-shaped MoE layer, hidden 2048, 64 routed experts top-6
 x ~ N(0,1), weights ~ N(0,0.02), seed 0. One step = one full layer forward
 (router -> grouping + gather -> expert FFN -> combine) through the public API.
 The weights (1.1 GB) exceed the 126 MB L2, so no flush is needed between
-steps. At N > 1 the experts are sharded evenly across ranks (expert parallel,
-NCCL all-to-all), each rank holding its own T tokens.
+steps. At N > 1 the experts are sharded evenly across ranks (expert parallel),
+each rank holding its own T tokens; rows move by NVLink stores into the
+owners' buffers (`--ep-transport peer`, the default) or by NCCL all-to-all
+(`--ep-transport nccl`). Before anything is timed, the step's output is
+checked on a sample of tokens against an f32 computation of the same layer
+with the reference's own bar; a step that disagrees is refused, not timed.
 
 Other configs: `--config c3` (config 3: routed experts int8 weight-only with
 bf16 per-channel scales, shared expert bf16; reports the weight footprint),
@@ -16,10 +20,13 @@ bf16 per-channel scales, shared expert bf16; reports the weight footprint),
 with the sigmoid group-limited router (8 groups, top-4 groups), intermediate
 2048, 1 shared expert, int8 routed experts, T = 8192 per GPU).
 
-`--impl reference` times the reference algorithm's CPU restatement (the
-oracle: the reference is pure PyTorch + Triton with no CPU code to compile,
-and cannot travel to the GPU box) on a bounded sample of the same workload
-with all host threads.
+`--impl reference` times the reference's own CPU path on a bounded sample of
+the same workload (CPU_SAMPLE_TOKENS tokens) with all host threads: its
+ReferenceMoE.forward (config 2) or its int8 grouped_moe_routed_quantized with
+torch_grouped_matmul_dequant (config 3), imported from the offline install of
+the reference under baseline/_ref; where that install is absent, the numpy
+restatement of the same algorithm (oracle/). The B200 line's `cpu_baseline`
+is the same measurement.
 """
 
 from __future__ import annotations
@@ -184,6 +191,10 @@ def barrier(world: int) -> None:
 
 
 # ---------------------------------------------------------------- CPU arms
+# Tokens per CPU forward, for the reference arm and the B200 line's cpu_baseline alike.
+CPU_SAMPLE_TOKENS = 128
+
+
 def oracle_weights(wl: Workload, rng):
     """f32 weights for the oracle (int8 configs: quantised and dequantised)."""
     import numpy as np
@@ -203,30 +214,92 @@ def oracle_weights(wl: Workload, rng):
     return router, gate, up, down, shared
 
 
-def oracle_forward(wl: Workload, x, weights):
+def import_reference_kernels():
+    """The reference's own kernel modules (its offline install under
+    baseline/_ref when it is not on sys.path), or None."""
+    try:
+        from dispatch.kernels import moe_forward, quantization, reference_moe  # noqa: PLC0415
+    except ImportError:
+        ref = ROOT / "baseline" / "_ref"
+        if not (ref / "dispatch").is_dir():
+            return None
+        sys.path.insert(0, str(ref))
+        try:
+            from dispatch.kernels import moe_forward, quantization, reference_moe  # noqa: PLC0415
+        except ImportError:
+            return None
+    return reference_moe, moe_forward, quantization
+
+
+def cpu_layer(wl: Workload, t_sample: int):
+    """A zero-argument CPU forward of the workload on t_sample tokens, its
+    kind ("reference": the reference's own code; "port": the numpy oracle)
+    and a description. Weights ~N(0, 0.02), x ~N(0, 1), seed 0."""
+    mods = import_reference_kernels()
+    if mods is not None and wl.router == "softmax":
+        import torch
+
+        reference_moe, moe_forward, quantization = mods
+        cfg = reference_moe.MoEConfig(hidden_size=wl.H, moe_intermediate_size=wl.I, n_routed_experts=wl.E,
+                                      n_shared_experts=wl.I_s // wl.I, num_experts_per_tok=wl.k)
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            m = reference_moe.ReferenceMoE(cfg).eval()
+        finally:
+            torch.set_default_dtype(prev)
+        g = torch.Generator().manual_seed(0)
+        with torch.no_grad():
+            for prm in m.parameters():
+                prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+        x = torch.randn(t_sample, wl.H, generator=g).to(torch.bfloat16)
+        if not wl.int8:
+            def fn():
+                with torch.no_grad():
+                    return m(x)
+
+            return fn, "reference", "ReferenceMoE.forward in bf16 (src/dispatch/kernels/reference_moe.py:74-78)"
+        q = quantization.quantize_stacked_weights(moe_forward.stack_expert_weights(m.experts))
+
+        def fn():
+            with torch.no_grad():
+                idx, w = m.route(x)
+                out = quantization.grouped_moe_routed_quantized(x, idx, w, q, quantization.torch_grouped_matmul_dequant)
+                return out + m.shared_experts(x)
+
+        return fn, "reference", ("ReferenceMoE.route + grouped_moe_routed_quantized(torch_grouped_matmul_dequant) "
+                                 "+ shared ExpertMLP in bf16 (src/dispatch/kernels/quantization.py:81-107)")
+    import numpy as np
+
     from oracle import moe_oracle as O
 
-    router, gate, up, down, shared = weights
-    return O.moe_forward(x, router, gate, up, down, wl.k, shared=shared, renormalize=wl.renorm)
+    rng = np.random.default_rng(0)
+    router, gate, up, down, shared = oracle_weights(wl, rng)
+    x = rng.standard_normal((t_sample, wl.H), dtype=np.float32)
+
+    def fn():
+        return O.moe_forward(x, router, gate, up, down, wl.k, shared=shared, renormalize=wl.renorm)
+
+    return fn, "port", "numpy restatement of the reference forward (oracle/moe_oracle.py), f32"
 
 
 def cpu_sample(wl: Workload, t_sample: int, seconds: float, min_reps: int):
-    import numpy as np
+    """Mean seconds per CPU forward on t_sample tokens with all host threads."""
+    import torch
     from threadpoolctl import threadpool_limits
 
     cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    weights = oracle_weights(wl, rng)
-    x = rng.standard_normal((t_sample, wl.H), dtype=np.float32)
+    fn, kind, desc = cpu_layer(wl, t_sample)
+    torch.set_num_threads(cores)
     times = []
     with threadpool_limits(limits=cores):
-        oracle_forward(wl, x, weights)
+        fn()
         t0 = time.perf_counter()
         while time.perf_counter() - t0 < seconds or len(times) < min_reps:
             s = time.perf_counter()
-            oracle_forward(wl, x, weights)
+            fn()
             times.append(time.perf_counter() - s)
-    return statistics.mean(times), len(times), cores
+    return statistics.mean(times), len(times), cores, kind, desc
 
 
 def run_reference(args, wl: Workload) -> None:
@@ -234,33 +307,36 @@ def run_reference(args, wl: Workload) -> None:
     if rank != 0:
         return
     if wl.name == "c5":
-        print(json.dumps({"impl": "reference", "unavailable": "the f32 CPU oracle of config 5 needs ~45 GB of host "
-                          "memory for its 256 dequantised experts"}), flush=True)
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no DeepSeek-V3 (sigmoid group) "
+                          "router, and the f32 CPU restatement of config 5 needs ~45 GB of host memory"}),
+              flush=True)
         return
-    sec, reps, cores = cpu_sample(wl, args.ref_tokens, 0.0, args.warmup + args.steps)
-    value = args.ref_tokens / sec
+    t_sample = CPU_SAMPLE_TOKENS
+    sec, reps, cores, kind, desc = cpu_sample(wl, t_sample, 0.0, args.warmup + args.steps)
+    value = t_sample / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{wl.desc}; {args.ref_tokens}-token sample of the T={wl.tokens} step",
-                   "tokens_per_gpu": wl.tokens, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.ref_tokens} tokens x {reps} forwards of the numpy oracle (f32)"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if kind == "reference" else "f32",
+        "data": "synthetic",
+        "config": {"workload": f"{wl.desc}; {t_sample}-token sample of the T={wl.tokens} step",
+                   "tokens_per_gpu": wl.tokens, "sample_tokens": t_sample, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": f"{reps} forwards of {t_sample} tokens: {desc}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def cpu_baseline_sample(wl: Workload, seconds: float = 12.0) -> dict:
-    """The oracle's forward on a bounded sample, rank 0 / N=1 only."""
+    """The reference arm's measurement, rank 0 / N=1 only."""
     if wl.name == "c5":
         return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                "sample": "skipped: the f32 oracle of config 5 needs ~45 GB of host memory"}
-    t_sample = 128
-    sec, reps, cores = cpu_sample(wl, t_sample, seconds, 2)
-    return {"value": t_sample / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{reps} x {t_sample}-token forwards of the numpy oracle (f32, all experts resident)"}
+                "sample": "skipped: no reference router for config 5, and its f32 restatement needs ~45 GB"}
+    t_sample = CPU_SAMPLE_TOKENS
+    sec, reps, cores, kind, desc = cpu_sample(wl, t_sample, seconds, 2)
+    return {"value": t_sample / sec, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{reps} forwards of {t_sample} tokens: {desc}"}
 
 
 # ---------------------------------------------------------------- B200 arm
@@ -311,6 +387,46 @@ def weight_footprint(ws) -> int:
         return sum(q.data.numel() * q.data.element_size() + q.scale.numel() * q.scale.element_size()
                    for q in (ws.gate, ws.up, ws.down))
     return sum(w.numel() * w.element_size() for w in (ws.gate, ws.up, ws.down))
+
+
+def check_layer_output(x, out, router, ws, sh, cfg, bias, n_rows: int = 64) -> dict:
+    """Refuse-to-time gate (the reference's run_kernel_bench.py:90,169-175 and
+    run_engine_race.py refuse a backend that disagrees with the reference):
+    n_rows tokens spread over the batch are recomputed in f32 on the GPU from
+    the same routing (router ids and weights are batch-invariant) and the
+    layer's output rows must pass the reference's assert_matches_reference
+    bar (rtol 1.6e-2, atol 1.6e-2 * max|ref|) and, for bf16 experts, also
+    rtol 2e-2 / atol 1e-2. Raises AssertionError otherwise."""
+    import torch
+
+    from dispatch_b200.kernels.layer import route
+    from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights
+
+    t = x.shape[0]
+    rows = torch.linspace(0, t - 1, min(n_rows, t), device=x.device).round().long().unique()
+    idx, w = route(x, router, cfg, e_score_bias=bias)
+    idx, w = idx[rows].long(), w[rows]
+    xf = x[rows].float()
+    quant = isinstance(ws, QuantizedStackedExpertWeights)
+
+    def mat(m, e):
+        return m.data[e].float() * m.scale[e].float()[:, None] if quant else m[e].float()
+
+    ref = torch.zeros(rows.numel(), x.shape[1], device=x.device)
+    for e in torch.unique(idx).tolist():
+        r, sl = (idx == e).nonzero(as_tuple=True)
+        hh = torch.nn.functional.silu(xf[r] @ mat(ws.gate, e).T) * (xf[r] @ mat(ws.up, e).T)
+        ref.index_add_(0, r, (hh @ mat(ws.down, e).T) * w[r, sl, None])
+    if sh is not None:
+        sg, su, sd = (m.float() for m in (sh.gate, sh.up, sh.down))
+        ref += (torch.nn.functional.silu(xf @ sg.T) * (xf @ su.T)) @ sd.T
+    got = out[rows].float()
+    torch.testing.assert_close(got, ref, rtol=1.6e-2, atol=1.6e-2 * float(ref.abs().max()))
+    bar = "assert_matches_reference (rtol 1.6e-2, atol 1.6e-2*max) vs f32 on the dequantised int8 weights"
+    if not quant:  # bf16 layers also meet the north-star bf16 bar; int8 ones the reference int8 bar only
+        torch.testing.assert_close(got, ref, rtol=2e-2, atol=1e-2)
+        bar = "assert_matches_reference (rtol 1.6e-2, atol 1.6e-2*max) and rtol 2e-2/atol 1e-2 vs f32"
+    return {"rows": int(rows.numel()), "max_abs_err": round(float((got - ref).abs().max()), 5), "bar": bar}
 
 
 def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
@@ -388,6 +504,24 @@ def run_b200(args, wl: Workload) -> None:
     res = moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias)
     torch.cuda.synchronize()
     L.check_device_status(dev)
+    # refuse to time a step whose output disagrees with the f32 reference
+    try:
+        checked = check_layer_output(x, layer(x), router, ws, sh, cfg, bias)
+        torch.cuda.synchronize()
+        L.check_device_status(dev)
+        ok = 1.0
+    except AssertionError as exc:
+        checked, ok = {"refused": str(exc).splitlines()[0][:300]}, 0.0
+    if max_over_ranks(-ok, world) > -1.0:  # some rank failed the check
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "refused": True, "checked": checked}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            if hasattr(ep, "close"):
+                ep.close()
+            dist.destroy_process_group()
+        raise SystemExit(1)
 
     with ClockSampler(local) as clocks:
         ms = time_loop(lambda: layer(x), args.steps, args.warmup, world, stream)
@@ -400,11 +534,36 @@ def run_b200(args, wl: Workload) -> None:
     # the timed region, on copy streams that overlap the neighbouring steps
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(t, wl.H, dtype=torch.bfloat16).pin_memory()
-    n_e2e = max(args.steps // 2, 3)
+    # enough batches that filling and draining the copy pipeline stays under ~2% of the run
+    n_e2e = max(4 * args.steps, 50)
     e2e_ms = max_over_ranks(
         time_loop(lambda: run_host_batches(layer, [x_host] * n_e2e, [out_host] * n_e2e), 1, 1, world, stream),
         world) / n_e2e
     e2e_val = t * world / (e2e_ms * 1e-3)
+
+    # expert-parallel phase split: CUDA events between the phases of a call,
+    # mean over calls, max over ranks (names the limiter of the N-GPU step)
+    ep_phases = None
+    if ep is not None and hasattr(ep, "PHASES"):
+        n_ph = 20
+        ep.phase_events = []
+        for _ in range(n_ph):
+            layer(x)
+        torch.cuda.synchronize()
+        evs, ep.phase_events = ep.phase_events, None
+        per_call = len(ep.PHASES) + 1
+        dur = torch.zeros(len(ep.PHASES), dtype=torch.float64)
+        for c in range(n_ph):
+            marks = evs[c * per_call:(c + 1) * per_call]
+            for i in range(1, per_call):
+                dur[i - 1] += marks[i - 1][1].elapsed_time(marks[i][1]) / n_ph
+        if world > 1:
+            import torch.distributed as dist
+
+            dd = dur.to(dev)
+            dist.all_reduce(dd, op=dist.ReduceOp.MAX)
+            dur = dd.cpu()
+        ep_phases = {name: round(float(v), 4) for name, v in zip(ep.PHASES, dur)}
 
     # dominant kernel: the gate/up tcgen05 GEMM (+SwiGLU epilogue), timed alone
     roof = gateup_roofline(wl, x, ws, sh, res, peaks, peak_kind, dev, stream)
@@ -446,6 +605,7 @@ def run_b200(args, wl: Workload) -> None:
                        "global_tokens": t * world, "routing": args.routing, "parallelism": parallelism,
                        "routed_weight_bytes": weight_footprint(ws),
                        "l2": "inputs larger than L2 (expert weights >= 1.1 GB per step)"},
+            "checked": checked,
             "layer_tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
             "roofline": roof,
             "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s", "h2d_bytes_per_step": t * wl.H * 2,
@@ -453,6 +613,7 @@ def run_b200(args, wl: Workload) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "sweep": sweep,
+            "ep_phases_ms": ep_phases,
             "peaks": {"kind": peak_kind, "hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"]},
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -469,6 +630,8 @@ def run_b200(args, wl: Workload) -> None:
 # DRAM bytes (read + write) of one gate/up launch on the C2 T=4096 step, from
 # an ncu capture of this kernel (dram__bytes_read.sum + dram__bytes_write.sum).
 GATEUP_TRAFFIC_C2 = 879.5e6 + 68.4e6
+GATEUP_TRAFFIC_SOURCE = ("ncu capture of this kernel on the C2 T=4096 step (dram__bytes_read.sum + "
+                         "dram__bytes_write.sum), profiles/grouped_gemm_c2_t4096.md; not measured in this run")
 
 
 def gateup_roofline(wl: Workload, x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
@@ -508,12 +671,14 @@ def gateup_roofline(wl: Workload, x, ws, sh, res, peaks, peak_kind, dev, stream)
     f1 = wl.gateup_flops(r, t)
     achieved = f1 / (ms1 * 1e-3) / 1e12
     f2 = wl.down_flops(r, t)
-    traffic = GATEUP_TRAFFIC_C2 if (wl.name == "c2" and t == 4096) else None
+    measured = wl.name == "c2" and t == 4096 and not quant
+    traffic = GATEUP_TRAFFIC_C2 if measured else None
     kernel = "grouped_gemm_kernel<int8> gate/up + SwiGLU" if quant else "grouped_gemm_kernel<bf16> gate/up + SwiGLU"
     return {"kernel": kernel + " (routed + shared)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 4), "peak_kind": f"{peak_kind} burst",
             "launch_ms": round(ms1, 4), "flops_per_launch": f1, "traffic": traffic,
+            "traffic_source": GATEUP_TRAFFIC_SOURCE if measured else "not captured for this config",
             "down_gemm": {"launch_ms": round(ms2, 4), "achieved": round(f2 / (ms2 * 1e-3) / 1e12, 1)}}
 
 
@@ -526,7 +691,6 @@ def main() -> None:
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: the config's)")
     ap.add_argument("--routing", choices=["uniform", "zipf"], default="uniform")
-    ap.add_argument("--ref-tokens", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",

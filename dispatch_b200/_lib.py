@@ -27,6 +27,7 @@ MOE_ERR_BAD_EXPERT = 6
 MOE_ERR_BAD_OFFSETS = 7
 
 DT_BF16, DT_F16, DT_F32, DT_I8, DT_I32, DT_I64 = range(6)
+FFN_KERNEL_AUTO, FFN_KERNEL_TILED, FFN_KERNEL_STREAM = range(3)
 ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
 
 _TORCH_DT = {
@@ -56,6 +57,7 @@ class MoeLayerDesc(ctypes.Structure):
 
 _SIGNATURES = {
     "moe_abi_version": ([], _i32),
+    "moe_set_ffn_kernel": ([_i32], _i32),
     "moe_status_string": ([_i32], ctypes.c_char_p),
     "moe_last_error": ([], ctypes.c_char_p),
     "moe_device_sm_count": ([], _i32),
@@ -116,7 +118,7 @@ _SIGNATURES = {
         _i32,
     ),
     "moe_ep_signal_bytes": ([_i32, _i64], _sz),
-    "moe_ep_exchange": ([_p, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _p], _i32),
+    "moe_ep_exchange": ([_p, _i64, _p, _p, _sz, _i32, _i32, _i32, _i32, _p, _p], _i32),
 }
 
 PEER_HANDLE_BYTES = 64

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <array>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -16,6 +17,7 @@
 #include "combine.cuh"
 #include "ep.cuh"
 #include "gemm.cuh"
+#include "gemm_stream.cuh"
 #include "group.cuh"
 #include "route.cuh"
 
@@ -186,13 +188,16 @@ struct SegSpec {
   void* const* out_table = nullptr;
   int out_table_n = 0;
   int64_t out_table_rows = 0;
+  // rows of the A (activation) TMA box: 128 for the tiled kernel, the row
+  // tile for the streaming kernel
+  int a_box_rows = moe::gemm::BM;
 };
 
 int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   std::memset(s, 0, sizeof(*s));
   // a gathered A is fetched one row per box, four boxes per tile::gather4
   int rc = sp.gather_rows ? make_map_a(&s->map_a, sp.a, act_dtype, sp.gather_src_rows, sp.K, sp.lda, 1)
-                          : make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda);
+                          : make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda, sp.a_box_rows);
   if (rc) return rc;
   const int box_rows = sp.swiglu ? sp.mma_n / 2 : sp.mma_n;
   const int64_t gw = sp.Gw > 0 ? sp.Gw : sp.G;
@@ -324,6 +329,76 @@ int run_gemm(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, 
   return any_i8 ? launch_gemm<true>(p, grid, stream) : launch_gemm<false>(p, grid, stream);
 }
 
+// ---------------------------------------------------------------- streaming kernel
+std::atomic<int> g_ffn_kernel{MOE_FFN_KERNEL_AUTO};
+
+// Largest dynamic shared memory of one CTA on sm_100 (227 KiB).
+constexpr size_t kMaxDynSmem = 232448;
+
+template <bool kInt8>
+int launch_stream(const moe::gemm::StreamParams& sp, int grid, size_t smem, cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_stream_kernel<kInt8>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxDynSmem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(stream gemm)");
+  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_stream_kernel<kInt8>, dim3(grid),
+                      dim3(moe::gemm::StreamConfig<kInt8>::kThreads), smem, stream, sp),
+           "grouped_gemm_stream_kernel launch");
+  return MOE_OK;
+}
+
+// The streaming kernel over up to two segments; row_tiles[i] (32 or 64) is
+// segment i's token rows per tile. Segments must be plain 16-bit-output GEMMs
+// with one K range and no gathered rows.
+int run_gemm_stream(const SegSpec* specs_in, const int* row_tiles, int nseg, int act_dtype, int32_t* status,
+                    cudaStream_t stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  moe::gemm::StreamParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  bool any_i8 = false;
+  int64_t tiles_bound = 0;
+  int nt_max = 0;
+  for (int i = 0; i < nseg; ++i) {
+    SegSpec spec = specs_in[i];
+    const int nt = row_tiles[i];
+    CHECK_ARG(nt % 32 == 0 && nt >= 32 && nt <= moe::gemm::kStreamMaxRowTile, "row tile %d not in {32, 64}", nt);
+    CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows,
+              "the streaming kernel takes plain 16-bit-output segments");
+    spec.mma_n = moe::gemm::SM_ROWS;
+    spec.a_box_rows = nt;
+    rc = check_seg(spec, act_dtype);
+    if (rc) return rc;
+    rc = fill_segment(&sp.p.seg[i], spec, act_dtype);
+    if (rc) return rc;
+    sp.row_tile[i] = nt;
+    nt_max = nt > nt_max ? nt : nt_max;
+    any_i8 |= spec.b_dtype == MOE_DT_I8;
+    const int oc = spec.swiglu ? moe::gemm::SM_ROWS / 2 : moe::gemm::SM_ROWS;
+    const int64_t rt = spec.offsets ? spec.a_rows / nt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
+                                    : (spec.a_rows + nt - 1) / nt;
+    tiles_bound += rt * ((spec.N + oc - 1) / oc);
+    sp.p.remote_out |= spec.out_rows ? 1 : 0;
+  }
+  sp.p.num_segs = nseg;
+  sp.p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
+  sp.p.status = status;
+  sp.nt_max = nt_max;
+  const size_t stage = moe::gemm::stream_stage_bytes(any_i8, nt_max);
+  size_t stages = (kMaxDynSmem - moe::gemm::stream_fixed_bytes()) / stage;
+  if (stages > static_cast<size_t>(moe::gemm::kStreamMaxStages)) stages = moe::gemm::kStreamMaxStages;
+  CHECK_ARG(stages >= 2, "streaming kernel: stages do not fit shared memory");
+  sp.stages = static_cast<int>(stages);
+  const size_t smem = moe::gemm::stream_fixed_bytes() + stages * stage;
+  const int grid = static_cast<int>(tiles_bound < sms ? tiles_bound : sms);
+  if (grid <= 0) return MOE_OK;
+  return any_i8 ? launch_stream<true>(sp, grid, smem, stream) : launch_stream<false>(sp, grid, smem, stream);
+}
+
 // Most K ranges the router's logit GEMM is split into (f32 slabs in the
 // router workspace).
 constexpr int kRouteMaxSplits = moe::route::kMaxSplits;
@@ -335,11 +410,36 @@ int route_tb(int64_t H, int E, bool computing) {
   return tb;
 }
 
+// The grouping's two launches (histogram, then scatter + gather). Copies of
+// 16-bit rows are split by column slices (at least 128 bytes of a row per CTA)
+// over more CTAs so the gather uses the whole GPU (about four CTAs per SM:
+// 0.651 -> 0.647 ms for the C2 T=4096 step against two) even for a decode
+// step's few rows.
+int launch_grouping(const moe::group::Params& p, int sms, cudaStream_t s) {
+  unsigned split = 1;
+  if (p.xs && p.x_dtype != MOE_DT_F32) {
+    const int64_t per_row = p.H / 8;
+    while (split < 32 && static_cast<int64_t>(p.nchunks) * split < 4 * sms && per_row % (2 * split) == 0 &&
+           per_row / (2 * split) >= 8)
+      split *= 2;
+  }
+  CUDA_TRY(launch_pdl(moe::group::group_hist_kernel, dim3(p.nchunks), dim3(moe::group::kThreads), 0, s, p),
+           "group_hist_kernel launch");
+  CUDA_TRY(launch_pdl(moe::group::group_scatter_kernel, dim3(p.nchunks, split), dim3(moe::group::kThreads), 0, s, p),
+           "group_scatter_kernel launch");
+  return MOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
 int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+int moe_set_ffn_kernel(int choice) {
+  if (choice != MOE_FFN_KERNEL_AUTO && choice != MOE_FFN_KERNEL_TILED && choice != MOE_FFN_KERNEL_STREAM) return -1;
+  return g_ffn_kernel.exchange(choice);
+}
 
 const char* moe_status_string(int code) {
   switch (code) {
@@ -376,6 +476,7 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   if (rc) return rc;
   CHECK_ARG(T >= 0 && E >= 1 && E <= moe::route::kMaxE, "E=%lld must be in [1, %d]", (long long)E, moe::route::kMaxE);
   CHECK_ARG(k >= 1 && k <= moe::route::kMaxK && k <= E, "top_k=%d must be in [1, min(E, %d)]", k, moe::route::kMaxK);
+  if (T == 0) return MOE_OK;  // nothing to route (empty tensors may come with null pointers)
   CHECK_ARG(topk_idx && topk_w, "null output pointer");
   CHECK_ARG(logits_in || (x && router_w && H >= 1), "need logits_in or x and router_w");
   if (!logits_in) {
@@ -480,7 +581,7 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
   CHECK_ARG(E >= 1 && E <= moe::group::kMaxE, "E=%lld must be in [1, %d]", (long long)E, moe::group::kMaxE);
   CHECK_ARG(k >= 1 && T >= 0, "bad T/k");
   CHECK_ARG(idx_dtype == MOE_DT_I32 || idx_dtype == MOE_DT_I64, "topk_idx must be int32 or int64");
-  CHECK_ARG(counts && offsets && pos, "null output pointer");
+  CHECK_ARG(counts && offsets && (pos || T == 0), "null output pointer");
   CHECK_ARG(!sorted_weight || topk_w, "sorted_weight needs topk_w");
   CHECK_ARG(workspace && workspace_bytes >= moe_group_workspace_bytes(T, k, E), "workspace too small");
   if (xs) {
@@ -516,23 +617,7 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
   p.xs_f16 = xs_dtype == MOE_DT_F16;
   p.hist = static_cast<int32_t*>(workspace);
   p.status = status;
-  // Copies of 16-bit rows are split by column slices (at least 128 bytes of
-  // a row per CTA) over more CTAs so the gather uses the whole GPU (about four
-  // CTAs per SM: 0.651 -> 0.647 ms for the C2 T=4096 step against two) even
-  // for a decode step's few rows.
-  unsigned split = 1;
-  if (xs && x_dtype != MOE_DT_F32) {
-    const int64_t per_row = H / 8;
-    while (split < 32 && static_cast<int64_t>(p.nchunks) * split < 4 * sms && per_row % (2 * split) == 0 &&
-           per_row / (2 * split) >= 8)
-      split *= 2;
-  }
-  CUDA_TRY(launch_pdl(moe::group::group_hist_kernel, dim3(p.nchunks), dim3(moe::group::kThreads), 0, s, p),
-           "group_hist_kernel launch");
-  CUDA_TRY(launch_pdl(moe::group::group_scatter_kernel, dim3(p.nchunks, split), dim3(moe::group::kThreads), 0, s, p),
-           "group_scatter_kernel launch");
-  CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
-  return MOE_OK;
+  return launch_grouping(p, sms, s);
 }
 
 }  // extern "C"
@@ -544,28 +629,26 @@ int moe_group_tokens(const void* topk_idx, int idx_dtype, const float* topk_w, i
 static __device__ __align__(256) int32_t g_group_scratch[MOE_GROUP_NOALLOC_SCRATCH_INTS];
 
 namespace {
-struct ScratchSlot {
-  std::once_flag once;
-  int32_t* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-std::array<ScratchSlot, kMaxDevices> g_scratch;
+std::mutex g_scratch_mu;
+std::array<int32_t*, kMaxDevices> g_scratch{};
 
 // Device address of g_group_scratch on the current device. On the host the
-// symbol name is only a stand-in, so the address is looked up once per
-// device, with that device current, on the first call.
+// symbol name is only a stand-in, so the address is looked up per device,
+// with that device current, and kept once a lookup has succeeded; a failed
+// lookup (say, one attempted during a stream capture) is reported and tried
+// again on the next call.
 int group_scratch(int32_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(MOE_ERR_NO_DEVICE, "no CUDA device is current");
-  ScratchSlot& slot = g_scratch[dev];
-  std::call_once(slot.once, [&] {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch[dev] == nullptr) {
     void* p = nullptr;
-    slot.err = cudaGetSymbolAddress(&p, g_group_scratch);
-    slot.ptr = static_cast<int32_t*>(p);
-  });
-  if (slot.err != cudaSuccess || slot.ptr == nullptr) return cuda_fail(slot.err, "cudaGetSymbolAddress(group scratch)");
-  *out = slot.ptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_group_scratch);
+    if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(group scratch)");
+    g_scratch[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_scratch[dev];
   return MOE_OK;
 }
 }  // namespace
@@ -588,7 +671,7 @@ int moe_group_tokens_noalloc(const void* topk_idx, int idx_dtype, const float* t
             "(T*k=%lld, E=%lld); use moe_group_tokens with a caller workspace",
             (long long)(chunks * E), MOE_GROUP_NOALLOC_SCRATCH_INTS, (long long)n, (long long)E);
   CHECK_ARG(idx_dtype == MOE_DT_I32 || idx_dtype == MOE_DT_I64, "topk_idx must be int32 or int64");
-  CHECK_ARG(counts && offsets && pos, "null output pointer");
+  CHECK_ARG(counts && offsets && (pos || T == 0), "null output pointer");
   CHECK_ARG(!sorted_weight || topk_w, "sorted_weight needs topk_w");
   if (xs) {
     CHECK_ARG(x && H >= 8 && H % 8 == 0, "gather needs x and H a multiple of 8");
@@ -627,11 +710,7 @@ int moe_group_tokens_noalloc(const void* topk_idx, int idx_dtype, const float* t
   // so the scratch needs no clearing between calls.
   p.hist = scratch;
   p.status = status;
-  moe::group::group_hist_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
-  CUDA_TRY(cudaGetLastError(), "group_hist_kernel launch");
-  moe::group::group_scatter_kernel<<<p.nchunks, moe::group::kThreads, 0, s>>>(p);
-  CUDA_TRY(cudaGetLastError(), "group_scatter_kernel launch");
-  return MOE_OK;
+  return launch_grouping(p, sms, s);
 }
 
 int moe_grouped_gemm(const void* a, int a_dtype, int64_t M, int64_t K, const void* w, int w_dtype,
@@ -674,6 +753,15 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                                 shared_gate, shared_up, shared_down, y, y_shared, workspace, workspace_bytes, status,
                                 stream);
 }
+
+// Automatic FFN kernel choice: the streaming kernel when the routed groups
+// average at most this many rows and the shared expert has at most this many.
+// Measured on B200 (C2 layer as a CUDA graph, fraction of HBM bandwidth,
+// tiled -> streaming): T=1 0.230 -> 0.283, T=16 0.659 -> 0.754, T=64 0.708 ->
+// 0.737, T=128 0.721 -> 0.700, T=512 0.687 -> 0.602; C3 (int8) T=1 0.119 ->
+// 0.180, T=16 0.263 -> 0.338, T=128 0.319 -> 0.317.
+constexpr int64_t kStreamMaxAvgRows = 8;
+constexpr int64_t kStreamMaxSharedRows = 96;
 
 // Where the routed down projection stores its rows: y, or scattered through
 // a table of (possibly peer) return buffers.
@@ -735,6 +823,28 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     ++n;
   }
   if (n == 0) return MOE_OK;
+  // Kernel choice (same bits either way): the streaming kernel when the
+  // routed groups average few rows and the shared expert's batch is small.
+  const int choice = g_ffn_kernel.load();
+  const bool streamable = !gather_rows;
+  bool use_stream = false;
+  if (choice == MOE_FFN_KERNEL_STREAM) {
+    CHECK_ARG(streamable, "the streaming kernel does not take gathered rows");
+    use_stream = true;
+  } else if (choice == MOE_FFN_KERNEL_AUTO && streamable) {
+    use_stream = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
+  }
+  if (use_stream) {
+    int nts[2];
+    int i = 0;
+    if (R > 0) nts[i++] = R <= 16 * G ? 32 : 64;
+    if (has_shared) nts[i++] = T_shared <= 32 ? 32 : 64;
+    if (part & 1) {
+      int rc = run_gemm_stream(g1, nts, n, act_dtype, status, s);
+      if (rc) return rc;
+    }
+    return (part & 2) ? run_gemm_stream(g2, nts, n, act_dtype, status, s) : MOE_OK;
+  }
   if (part & 1) {
     int rc = run_gemm(g1, n, act_dtype, status, s);
     if (rc) return rc;
@@ -774,9 +884,9 @@ int moe_combine(const void* y, int y_dtype, const int32_t* pos, const float* top
   CHECK_ARG(H % 8 == 0, "H=%lld must be a multiple of 8", (long long)H);
   CHECK_ARG(y_dtype == MOE_DT_BF16 || y_dtype == MOE_DT_F16 || y_dtype == MOE_DT_F32, "bad y dtype");
   CHECK_ARG(out_dtype == MOE_DT_BF16 || out_dtype == MOE_DT_F16 || out_dtype == MOE_DT_F32, "bad out dtype");
-  CHECK_ARG(out && (T == 0 || (y && pos && topk_w)), "null pointer");
+  if (T == 0) return MOE_OK;  // nothing to combine (empty tensors may come with null pointers)
+  CHECK_ARG(out && y && pos && topk_w, "null pointer");
   CHECK_ARG(aligned16(y) && aligned16(out) && aligned16(y_shared), "y/out must be 16-byte aligned");
-  if (T == 0) return MOE_OK;
   moe::combine::Params p;
   p.y = y;
   p.y_shared = y_shared;
@@ -1046,8 +1156,9 @@ size_t moe_ep_signal_bytes(int world, int64_t n) {
   return MOE_EP_SIGNAL_HEADER_BYTES + static_cast<size_t>(world) * static_cast<size_t>(n) * sizeof(int32_t);
 }
 
-int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal, int slot,
-                    int rank, int world, int32_t epoch, int32_t* status, void* stream) {
+int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal,
+                    size_t signal_bytes, int slot, int rank, int world, int32_t epoch, int32_t* status,
+                    void* stream) {
   int sms = 0;
   int rc = device_info(&sms);
   if (rc) return rc;
@@ -1056,6 +1167,9 @@ int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal,
   CHECK_ARG(slot >= 0 && slot < MOE_EP_FLAG_SLOTS, "flag slot %d not in [0, %d)", slot, MOE_EP_FLAG_SLOTS);
   CHECK_ARG(n >= 0 && (n == 0 || payload), "payload of %lld int32 needs a pointer", (long long)n);
   CHECK_ARG(peer_signal && local_signal, "null signal buffer");
+  CHECK_ARG(moe_ep_signal_bytes(world, n) <= signal_bytes,
+            "signal buffers of %zu bytes cannot hold the header and a (%d, %lld) int32 payload (%zu bytes)",
+            signal_bytes, world, (long long)n, moe_ep_signal_bytes(world, n));
   moe::ep::ExchangeParams p;
   p.payload = payload;
   p.n = n;

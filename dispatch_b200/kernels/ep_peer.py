@@ -71,6 +71,7 @@ class PeerBuffers:
             sizes = (self.recv_cap * hidden * 2, self.recv_cap * 4, self.back_rows * hidden * 2,
                      lib.moe_ep_signal_bytes(world, n_experts))
             nb = len(sizes)
+            self.signal_bytes = sizes[3]
             handles = (ctypes.c_uint8 * (nb * L.PEER_HANDLE_BYTES))()
             for i, n in enumerate(sizes):
                 p = ctypes.c_void_p()
@@ -118,8 +119,8 @@ class PeerBuffers:
         n = 0 if payload is None else payload.numel()
         epoch = ((epoch + 2**31) % 2**32) - 2**31  # the kernel compares int32 epochs wrap-safely
         rc = self._lib.moe_ep_exchange(
-            None if payload is None else payload.data_ptr(), n, self.t_signal.data_ptr(), self.signal_ptr, slot,
-            self.rank, self.world, epoch, L.status_word(dev).data_ptr(), L.stream_ptr(dev))
+            None if payload is None else payload.data_ptr(), n, self.t_signal.data_ptr(), self.signal_ptr,
+            self.signal_bytes, slot, self.rank, self.world, epoch, L.status_word(dev).data_ptr(), L.stream_ptr(dev))
         L.check(rc, "moe_ep_exchange")
 
     def close(self) -> None:
@@ -189,6 +190,18 @@ class PeerEPLayer:
         self._side: torch.cuda.Stream | None = None
         # launches of this library per call: route x2, group x2, exchange x3, dispatch, FFN x2 (+2 shared), combine
         self.launches_per_step = 13 if self.overlap_shared else 11
+        # Set to a list to have each call append (phase name, CUDA event)
+        # marks, recorded on the current stream after each phase.
+        self.phase_events: list | None = None
+
+    PHASES = ("route_group", "count_exchange", "dispatch", "barrier_after_dispatch", "ffn_and_return",
+              "barrier_after_ffn", "combine")
+
+    def _mark(self, name: str) -> None:
+        if self.phase_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_events.append((name, ev))
 
     def launches_for(self, t: int) -> int:
         """Launches of this library in one call on t tokens."""
@@ -233,8 +246,10 @@ class PeerEPLayer:
         st = L.status_word(dev).data_ptr()
         stream = L.stream_ptr(dev)
         k = self.top_k
+        self._mark("start")
         idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
         counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
+        self._mark("route_group")
         sh = self.shared
         i_sh = 0 if sh is None else sh.gate.shape[0]
         ys = torch.empty(t, h, dtype=x.dtype, device=dev) if sh is not None else None
@@ -254,13 +269,16 @@ class PeerEPLayer:
         buf.epoch += 1
         epoch = buf.epoch
         buf.exchange(counts, 0, epoch)
+        self._mark("count_exchange")
         rc = lib.moe_ep_dispatch(
             x.data_ptr(), L.dt(x), t, h, idx.data_ptr(), L.dt(idx), k, pos.data_ptr(), offsets.data_ptr(),
             buf.counts_all_ptr, self.rank, self.world, self.n_experts, buf.t_recv.data_ptr(),
             buf.t_ret.data_ptr(), buf.recv_cap, buf.recv_offsets.data_ptr(), st, stream,
         )
         L.check(rc, "moe_ep_dispatch")
+        self._mark("dispatch")
         buf.exchange(None, 1, epoch)
+        self._mark("barrier_after_dispatch")
         fused_shared = sh is not None and not overlap
         wq = self.weights
         g, u, d = (wq.gate.data, wq.up.data, wq.down.data) if self.quant else (wq.gate, wq.up, wq.down)
@@ -278,11 +296,14 @@ class PeerEPLayer:
             ws.numel(), st, stream,
         )
         L.check(rc, "moe_ep_expert_ffn")
+        self._mark("ffn_and_return")
         buf.exchange(None, 2, epoch)
+        self._mark("barrier_after_ffn")
         if shared_done is not None:
             torch.cuda.current_stream(dev).wait_event(shared_done)
         out = torch.empty(t, h, dtype=x.dtype, device=dev)
         rc = lib.moe_combine(buf.back_ptr, L.dt(x), pos.data_ptr(), wf.data_ptr(), t, k, h, L.ptr(ys),
                              out.data_ptr(), L.dt(out), st, stream)
         L.check(rc, "moe_combine")
+        self._mark("combine")
         return out

@@ -219,6 +219,10 @@ def run_host_batches(fn, inputs: list[torch.Tensor], outputs: list[torch.Tensor]
     comp = torch.cuda.current_stream(dev)
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     slots = [torch.empty(inputs[0].shape, dtype=inputs[0].dtype, device=dev) for _ in range(2)]
+    # The slots come from the compute stream's pool: the caching allocator may
+    # hand back memory that kernels already queued there still read, so the
+    # copy stream starts after everything queued on the compute stream so far.
+    h2d.wait_stream(comp)
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     snaps: list[torch.Tensor | None] = [None, None]  # private copies of the results

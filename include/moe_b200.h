@@ -10,7 +10,8 @@
  * int32 status word in device memory (first error wins; 0 = OK); the caller
  * reads it after synchronising. Calls are stream-ordered and thread-compatible:
  * one stream per call, no global mutable state apart from a per-device cache
- * of the SM count and the driver's tensor-map encoder.
+ * of the SM count and the driver's tensor-map encoder, and the process-wide
+ * FFN kernel choice of moe_set_ffn_kernel.
  *
  * Layouts (row-major, contiguous unless a leading dimension is passed):
  *   x            (T, H)        activations, bf16 / f16 / f32
@@ -53,6 +54,29 @@ extern "C" {
 #define MOE_DT_I8 3
 #define MOE_DT_I32 4
 #define MOE_DT_I64 5
+
+/*
+ * Which grouped-GEMM kernel the expert-FFN entry points (moe_expert_ffn,
+ * moe_expert_ffn_part, moe_expert_ffn_grouped, moe_ep_expert_ffn,
+ * moe_layer_forward) launch:
+ *   MOE_FFN_KERNEL_TILED   128 token rows x 256 weight columns per tile
+ *                          (prefill-sized groups);
+ *   MOE_FFN_KERNEL_STREAM  128 weight rows x 32 or 64 token rows per tile,
+ *                          up to 12 stages of weights in flight per SM
+ *                          (decode-sized groups: streams the weights);
+ *   MOE_FFN_KERNEL_AUTO    (default) STREAM when the routed groups average at
+ *                          most 8 rows and the shared expert has at most 96,
+ *                          else TILED.
+ * Both kernels give every row the same bits (same k-block order; the tensor
+ * cores' result does not depend on operand orientation), so the choice
+ * changes speed only. Process-wide; returns the previous choice, or -1 for an
+ * unknown one (nothing changes). No reference counterpart: the reference's
+ * tile size is the caller's block_m (src/dispatch/kernels/tile_schedule.py).
+ */
+#define MOE_FFN_KERNEL_AUTO 0
+#define MOE_FFN_KERNEL_TILED 1
+#define MOE_FFN_KERNEL_STREAM 2
+int moe_set_ffn_kernel(int choice);
 
 /* router modes */
 #define MOE_ROUTER_SOFTMAX 0        /* softmax top-k (optionally renormalised) */

@@ -120,7 +120,11 @@ int moe_ep_expert_ffn(const void* recv, int act_dtype, int64_t recv_cap, int64_t
  * A signal buffer (moe_ep_signal_bytes, from moe_peer_alloc, zero at
  * allocation) holds MOE_EP_FLAG_SLOTS rows of MOE_EP_MAX_RANKS int32 flags
  * in its first MOE_EP_SIGNAL_HEADER_BYTES, then a (world, n) int32 payload
- * area. One launch (a single CTA) on this rank: copies `payload` (n int32, may
+ * area. `signal_bytes` is the size of every rank's signal buffer (all ranks
+ * allocate the same size); a payload that does not fit, i.e.
+ * moe_ep_signal_bytes(world, n) > signal_bytes, is refused with
+ * MOE_ERR_INVALID_ARG before anything is stored into peer memory.
+ * One launch (a single CTA) on this rank: copies `payload` (n int32, may
  * be 0) into row `rank` of every rank's payload area, fences at system scope,
  * stores `epoch` into flag [slot][rank] of every rank (release), then waits
  * until flags [slot][0..world) of its own buffer are >= epoch (acquire).
@@ -132,8 +136,9 @@ int moe_ep_expert_ffn(const void* recv, int act_dtype, int64_t recv_cap, int64_t
 #define MOE_EP_SIGNAL_HEADER_BYTES 256
 #define MOE_EP_FLAG_SLOTS 4
 size_t moe_ep_signal_bytes(int world, int64_t n);
-int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal, int slot,
-                    int rank, int world, int32_t epoch, int32_t* status, void* stream);
+int moe_ep_exchange(const int32_t* payload, int64_t n, void* const* peer_signal, int32_t* local_signal,
+                    size_t signal_bytes, int slot, int rank, int world, int32_t epoch, int32_t* status,
+                    void* stream);
 
 #ifdef __cplusplus
 }

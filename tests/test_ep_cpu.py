@@ -253,7 +253,7 @@ def test_exchange_without_a_device_reports_it() -> None:
         pytest.skip("a GPU is present")
     from dispatch_b200 import _lib as L
 
-    rc = L.lib().moe_ep_exchange(None, 0, None, None, 0, 0, 1, 1, None, None)
+    rc = L.lib().moe_ep_exchange(None, 0, None, None, 0, 0, 0, 1, 1, None, None)
     assert rc == L.MOE_ERR_NO_DEVICE
 
 

@@ -34,9 +34,11 @@ def _signal(world: int, n: int) -> int:
     return p.value
 
 
-def _exchange(payload, n, table, sig, slot, rank, world, epoch) -> None:
-    rc = L.lib().moe_ep_exchange(None if payload is None else payload.data_ptr(), n, table.data_ptr(), sig, slot,
-                                 rank, world, epoch, L.status_word(DEV).data_ptr(), L.stream_ptr(DEV))
+def _exchange(payload, n, table, sig, slot, rank, world, epoch, sig_bytes=None) -> None:
+    sig_bytes = L.lib().moe_ep_signal_bytes(world, n) if sig_bytes is None else sig_bytes
+    rc = L.lib().moe_ep_exchange(None if payload is None else payload.data_ptr(), n, table.data_ptr(), sig,
+                                 sig_bytes, slot, rank, world, epoch, L.status_word(DEV).data_ptr(),
+                                 L.stream_ptr(DEV))
     L.check(rc, "moe_ep_exchange")
 
 
@@ -73,6 +75,22 @@ def test_exchange_wait_gives_up_with_timeout_status() -> None:
         # the context still works: a complete single-rank exchange afterwards
         one = torch.tensor([sig], dtype=torch.int64, device=DEV)
         _exchange(None, 0, one, sig, 2, 0, 1, 1)
+        torch.cuda.synchronize()
+        L.check_device_status(DEV)
+    finally:
+        torch.cuda.synchronize()
+        L.check(L.lib().moe_peer_free(sig), "moe_peer_free")
+
+
+def test_exchange_refuses_a_payload_larger_than_the_signal_buffers() -> None:
+    """A caller that passes more payload than the signal buffers hold gets an
+    argument error before anything is stored (the stores go to peer memory)."""
+    sig = _signal(1, 8)
+    try:
+        table = torch.tensor([sig], dtype=torch.int64, device=DEV)
+        payload = torch.zeros(16, dtype=torch.int32, device=DEV)
+        with pytest.raises(ValueError, match="cannot hold"):
+            _exchange(payload, 16, table, sig, 0, 0, 1, 1, sig_bytes=L.lib().moe_ep_signal_bytes(1, 8))
         torch.cuda.synchronize()
         L.check_device_status(DEV)
     finally:

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 from golden_inputs import c1_inputs, toy_inputs
-from gpu_helpers import LayerWeights, assert_parity, np32, randn
+from gpu_helpers import LayerWeights, assert_int8_parity, assert_parity, np32, randn
 
 from oracle import moe_oracle as O
 
@@ -89,8 +89,11 @@ def test_grouped_matmul_int8_matches_dequant_oracle(scale_dtype, sizes, n, k) ->
 
 
 def test_rows_do_not_depend_on_tile_width() -> None:
-    """A small launch uses narrower MMA tiles than a large one; the rows they
-    share must come out byte-identical (the property EP byte-exactness needs)."""
+    """A row's result must not depend on the launch it lands in: here the same
+    three rows computed inside a large launch (many tiles, other rows in their
+    128-row tiles) and alone (a three-tile launch) come out byte-identical --
+    the property EP byte-exactness needs, since an expert's rows arrive on
+    its owner in a different batch than on one GPU."""
     g = torch.Generator(device="cuda").manual_seed(5)
     e, n, k = 8, 1408, 2048
     w = randn((e, n, k), g, k ** -0.5)
@@ -373,27 +376,114 @@ def test_host_batches_overlap_copies_and_keep_the_bits(c2_weights: LayerWeights)
         assert torch.equal(o, o2)
 
 
-def test_layer_prefill_4096_vs_torch_fp32(c2_weights: LayerWeights) -> None:
-    """Full prefill size: checked against an f32 torch computation of the same
-    math on the GPU (a floating-point reference, not the oracle)."""
+def _torch_fp32_layer(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, expert, shared) -> torch.Tensor:
+    """The layer in f32 on the GPU (a floating-point reference for shapes whose
+    f32 numpy oracle does not fit in host memory): expert(e) -> (gate, up,
+    down) f32 matrices, shared = (gate, up, down) or None."""
+    xf = x.float()
+    out = torch.zeros(x.shape[0], x.shape[1], device=DEV)
+    for e in torch.unique(ids).tolist():
+        tok, slot = (ids == e).nonzero(as_tuple=True)
+        g_, u_, d_ = expert(e)
+        h = torch.nn.functional.silu(xf[tok] @ g_.T) * (xf[tok] @ u_.T)
+        out.index_add_(0, tok, (h @ d_.T) * w[tok, slot, None].float())
+    if shared is not None:
+        sg, su, sd = (s_.float() for s_ in shared)
+        out += (torch.nn.functional.silu(xf @ sg.T) * (xf @ su.T)) @ sd.T
+    return out
+
+
+@pytest.mark.parametrize("t", [1024, 4096])
+def test_layer_c2_prefill_vs_oracle(c2_weights: LayerWeights, t: int) -> None:
+    """C2 at prefill sizes against the numpy oracle: ids exact given the GPU's
+    logits, counts exact, output within both tolerance bars."""
     lw = c2_weights
-    g = torch.Generator(device="cuda").manual_seed(9)
-    x = randn((4096, 2048), g, 1.0)
+    g = torch.Generator(device="cuda").manual_seed(500 + t)
+    x = randn((t, 2048), g, 1.0)
     res = moe_layer_forward(x, lw.router, StackedExpertWeights(lw.gate, lw.up, lw.down), RouterConfig(top_k=6),
                             shared=SharedExpertWeights(*lw.shared))
-    ids = res.topk_idx.long()
-    w = res.topk_weight
-    xf = x.float()
-    out = torch.zeros(4096, 2048, device=DEV)
-    for e in range(64):
-        tok, slot = (ids == e).nonzero(as_tuple=True)
-        if tok.numel() == 0:
-            continue
-        h = torch.nn.functional.silu(xf[tok] @ lw.gate[e].float().T) * (xf[tok] @ lw.up[e].float().T)
-        out.index_add_(0, tok, (h @ lw.down[e].float().T) * w[tok, slot, None])
-    sg, su, sd = (s.float() for s in lw.shared)
-    out += (torch.nn.functional.silu(xf @ sg.T) * (xf @ su.T)) @ sd.T
-    assert_parity(res.out, out)
+    _, _, lg = route(x, lw.router, RouterConfig(top_k=6), return_logits=True)
+    ids, w = O.route_softmax_topk(lg.cpu().numpy(), 6)
+    np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), ids)
+    np.testing.assert_array_equal(res.group_sizes.cpu().numpy(), np.bincount(ids.reshape(-1), minlength=64))
+    assert_parity(res.out, _oracle_layer(np32(x), lw, 6, ids, w))
+
+
+@pytest.fixture(scope="module")
+def c3_weights(c2_weights: LayerWeights) -> QuantizedStackedExpertWeights:
+    lw = c2_weights
+    return QuantizedStackedExpertWeights(*(quantize_per_channel_int8(t, scale_dtype=torch.bfloat16)
+                                           for t in (lw.gate, lw.up, lw.down)))
+
+
+@pytest.mark.parametrize("t", [1024, 4096])
+def test_layer_c3_int8_prefill_vs_dequant_oracle(c2_weights: LayerWeights, c3_weights, t: int) -> None:
+    """C3 (int8 routed experts, bf16 scales, bf16 shared) at prefill sizes
+    against the oracle on the dequantised weights -- the reference int8 path's
+    own check (torch_grouped_matmul_dequant, quantization.py:81-107)."""
+    lw, qw = c2_weights, c3_weights
+    g = torch.Generator(device="cuda").manual_seed(600 + t)
+    x = randn((t, 2048), g, 1.0)
+    res = moe_layer_forward(x, lw.router, qw, RouterConfig(top_k=6), shared=SharedExpertWeights(*lw.shared))
+    _, _, lg = route(x, lw.router, RouterConfig(top_k=6), return_logits=True)
+    ids, w = O.route_softmax_topk(lg.cpu().numpy(), 6)
+    np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), ids)
+    deq = [O.dequantize_int8(q.data.cpu().numpy(), np32(q.scale)) for q in (qw.gate, qw.up, qw.down)]
+    out_ref, _, _ = O.moe_forward(np32(x), None, *deq, 6, shared=tuple(np32(s) for s in lw.shared), topk=(ids, w))
+    assert_parity(res.out, out_ref)
+
+
+C5_H, C5_E, C5_I, C5_IS = 7168, 256, 2048, 2048
+C5_ROUTER = RouterConfig(top_k=8, mode="sigmoid_group", renormalize=True, n_group=8, topk_group=4,
+                         routed_scaling_factor=2.5)
+
+
+@pytest.fixture(scope="module")
+def c5_layer():
+    """DeepSeek-V3-shaped layer (config 5): 256 routed experts int8 with bf16
+    per-channel scales (quantised on the device 32 experts at a time), one
+    bf16 shared expert, router bias for the group-limited sigmoid router."""
+    g = torch.Generator(device="cuda").manual_seed(55)
+    router = randn((C5_E, C5_H), g, 0.02)
+
+    def experts(n: int, k: int) -> QuantizedTensor:
+        qs, ss = [], []
+        for _ in range(0, C5_E, 32):
+            q = quantize_per_channel_int8(randn((32, n, k), g, 0.02), scale_dtype=torch.bfloat16)
+            qs.append(q.data)
+            ss.append(q.scale)
+        return QuantizedTensor(torch.cat(qs), torch.cat(ss))
+
+    qw = QuantizedStackedExpertWeights(experts(C5_I, C5_H), experts(C5_I, C5_H), experts(C5_H, C5_I))
+    sh = SharedExpertWeights(randn((C5_IS, C5_H), g, 0.02), randn((C5_IS, C5_H), g, 0.02),
+                             randn((C5_H, C5_IS), g, 0.02))
+    bias = (torch.randn(C5_E, generator=g, device="cuda") * 0.01).float()
+    return router, qw, sh, bias
+
+
+@pytest.mark.parametrize("t", [64, 1024])
+def test_layer_c5_deepseek_v3_int8_full_shape(c5_layer, t: int) -> None:
+    """Config 5 at full shape (H 7168, E 256 top-8 of 8 groups / top-4 groups,
+    int8 experts K=7168 and K=2048, one shared expert): ids exact against the
+    oracle's selection on the GPU's logits, output against an f32 computation
+    on the dequantised weights (the f32 numpy oracle would need ~45 GB) with
+    the reference int8 path's own bar."""
+    router, qw, sh, bias = c5_layer
+    g = torch.Generator(device="cuda").manual_seed(700 + t)
+    x = randn((t, C5_H), g, 1.0)
+    res = moe_layer_forward(x, router, qw, C5_ROUTER, shared=sh, e_score_bias=bias)
+    _, _, lg = route(x, router, C5_ROUTER, e_score_bias=bias, return_logits=True)
+    ids, w = O.route_sigmoid_grouped(lg.cpu().numpy(), bias.cpu().numpy(), 8, 8, 4, routed_scaling_factor=2.5)
+    np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), ids)
+    np.testing.assert_allclose(res.topk_weight.cpu().numpy(), w, rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(res.group_sizes.cpu().numpy(), np.bincount(ids.reshape(-1), minlength=C5_E))
+
+    def deq(qt: QuantizedTensor, e: int) -> torch.Tensor:
+        return qt.data[e].float() * qt.scale[e].float()[:, None]
+
+    ref = _torch_fp32_layer(x, res.topk_idx.long(), res.topk_weight,
+                            lambda e: (deq(qw.gate, e), deq(qw.up, e), deq(qw.down, e)), (sh.gate, sh.up, sh.down))
+    assert_int8_parity(res.out, ref)
 
 
 def test_grouped_moe_routed_reference_surface_toy_and_real() -> None:
