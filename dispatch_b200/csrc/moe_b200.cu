@@ -350,9 +350,17 @@ int launch_stream(const moe::gemm::StreamParams& sp, int grid, size_t smem, cuda
   return MOE_OK;
 }
 
-// The streaming kernel over up to two segments; row_tiles[i] (32 or 64) is
-// segment i's token rows per tile. Segments must be plain 16-bit-output GEMMs
-// with one K range and no gathered rows.
+// The streaming kernel over up to two segments; row_tiles[i] (a multiple of
+// 32, at most 256) is segment i's token rows per tile. Segments must be plain
+// 16-bit-output GEMMs with one K range and no gathered rows.
+//
+// Chains per tile (1 or 2 weight blocks sharing the tile's rows, their MMAs
+// interleaved): a single accumulator's dependent MMAs run at ~330 cycles each
+// on B200 whatever the MMA width, two interleaved chains at ~420 cycles per
+// pair, so two chains nearly double the tensor rate of a tile -- but halve
+// the tile count. Two chains are used unless that leaves the launch with
+// fewer tiles than SMs where one chain would have had several per SM
+// (estimated from the tile-count bound: waves x chain cost).
 int run_gemm_stream(const SegSpec* specs_in, const int* row_tiles, int nseg, int act_dtype, int32_t* status,
                     cudaStream_t stream) {
   int sms = 0;
@@ -361,12 +369,13 @@ int run_gemm_stream(const SegSpec* specs_in, const int* row_tiles, int nseg, int
   moe::gemm::StreamParams sp;
   std::memset(&sp, 0, sizeof(sp));
   bool any_i8 = false;
-  int64_t tiles_bound = 0;
+  int64_t tiles1 = 0, tiles2 = 0;  // tile-count bounds with one and with two chains
   int nt_max = 0;
   for (int i = 0; i < nseg; ++i) {
     SegSpec spec = specs_in[i];
     const int nt = row_tiles[i];
-    CHECK_ARG(nt % 32 == 0 && nt >= 32 && nt <= moe::gemm::kStreamMaxRowTile, "row tile %d not in {32, 64}", nt);
+    CHECK_ARG(nt % 32 == 0 && nt >= 32 && nt <= moe::gemm::kStreamMaxRowTile,
+              "row tile %d must be a multiple of 32 in [32, %d]", nt, moe::gemm::kStreamMaxRowTile);
     CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows,
               "the streaming kernel takes plain 16-bit-output segments");
     spec.mma_n = moe::gemm::SM_ROWS;
@@ -381,20 +390,27 @@ int run_gemm_stream(const SegSpec* specs_in, const int* row_tiles, int nseg, int
     const int oc = spec.swiglu ? moe::gemm::SM_ROWS / 2 : moe::gemm::SM_ROWS;
     const int64_t rt = spec.offsets ? spec.a_rows / nt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
                                     : (spec.a_rows + nt - 1) / nt;
-    tiles_bound += rt * ((spec.N + oc - 1) / oc);
+    const int64_t ct = (spec.N + oc - 1) / oc;
+    tiles1 += rt * ct;
+    tiles2 += rt * ((ct + 1) / 2);
     sp.p.remote_out |= spec.out_rows ? 1 : 0;
   }
+  const int64_t waves1 = (tiles1 + sms - 1) / sms, waves2 = (tiles2 + sms - 1) / sms;
+  const int chains = (waves2 * 420 <= waves1 * 330) ? 2 : 1;
   sp.p.num_segs = nseg;
   sp.p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
   sp.p.status = status;
   sp.nt_max = nt_max;
-  const size_t stage = moe::gemm::stream_stage_bytes(any_i8, nt_max);
+  sp.chains = chains;
+  sp.acc_slots = chains * nt_max * 2 <= 512 ? 2 : 1;
+  const size_t stage = moe::gemm::stream_stage_bytes(any_i8, nt_max, chains);
   size_t stages = (kMaxDynSmem - moe::gemm::stream_fixed_bytes()) / stage;
   if (stages > static_cast<size_t>(moe::gemm::kStreamMaxStages)) stages = moe::gemm::kStreamMaxStages;
   CHECK_ARG(stages >= 2, "streaming kernel: stages do not fit shared memory");
   sp.stages = static_cast<int>(stages);
   const size_t smem = moe::gemm::stream_fixed_bytes() + stages * stage;
-  const int grid = static_cast<int>(tiles_bound < sms ? tiles_bound : sms);
+  const int64_t tiles = chains == 2 ? tiles2 : tiles1;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   if (grid <= 0) return MOE_OK;
   return any_i8 ? launch_stream<true>(sp, grid, smem, stream) : launch_stream<false>(sp, grid, smem, stream);
 }
@@ -754,14 +770,13 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
                                 stream);
 }
 
-// Automatic FFN kernel choice: the streaming kernel when the routed groups
-// average at most this many rows and the shared expert has at most this many.
-// Measured on B200 (C2 layer as a CUDA graph, fraction of HBM bandwidth,
-// tiled -> streaming): T=1 0.230 -> 0.283, T=16 0.659 -> 0.754, T=64 0.708 ->
-// 0.737, T=128 0.721 -> 0.700, T=512 0.687 -> 0.602; C3 (int8) T=1 0.119 ->
-// 0.180, T=16 0.263 -> 0.338, T=128 0.319 -> 0.317.
-constexpr int64_t kStreamMaxAvgRows = 8;
-constexpr int64_t kStreamMaxSharedRows = 96;
+// Automatic FFN kernel choice: the streaming kernel for the gate/up
+// projection when the routed groups average at most this many rows and the
+// shared expert has at most this many. Measured on B200, C2 gate/up launch
+// (tiled -> streaming with two chains): T=1 54.4 -> 35.8 us, T=16 128.1 ->
+// 123.5 us, T=128 141.8 -> 175.8 us.
+constexpr int64_t kStreamMaxAvgRows = 2;
+constexpr int64_t kStreamMaxSharedRows = 32;
 
 // Where the routed down projection stores its rows: y, or scattered through
 // a table of (possibly peer) return buffers.
@@ -823,33 +838,33 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     ++n;
   }
   if (n == 0) return MOE_OK;
-  // Kernel choice (same bits either way): the streaming kernel when the
-  // routed groups average few rows and the shared expert's batch is small.
+  // Kernel choice per projection (every choice gives the same bits). AUTO:
+  // the streaming kernel for the gate/up projection of decode-sized batches
+  // (routed groups averaging at most kStreamMaxAvgRows rows, a shared expert
+  // of at most kStreamMaxSharedRows), the tiled kernel otherwise -- and for
+  // the down projection always, which the tiled kernel ran faster at every
+  // batch size measured (C2 T=1: 21 vs 33 us; T=16: 58 vs 89 us).
   const int choice = g_ffn_kernel.load();
   const bool streamable = !gather_rows;
-  bool use_stream = false;
-  if (choice == MOE_FFN_KERNEL_STREAM) {
-    CHECK_ARG(streamable, "the streaming kernel does not take gathered rows");
-    use_stream = true;
-  } else if (choice == MOE_FFN_KERNEL_AUTO && streamable) {
-    use_stream = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
-  }
-  if (use_stream) {
-    int nts[2];
+  CHECK_ARG(choice != MOE_FFN_KERNEL_STREAM || streamable, "the streaming kernel does not take gathered rows");
+  const bool small = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
+  const bool stream1 = choice == MOE_FFN_KERNEL_STREAM || (choice == MOE_FFN_KERNEL_AUTO && streamable && small);
+  const bool stream2 = choice == MOE_FFN_KERNEL_STREAM;
+  // row tile per segment for the streaming kernel: about the rows a group
+  // holds (routed: the average per group; shared: all of its rows), in [32, 256]
+  auto row_tile = [](int64_t rows) { return rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; };
+  int nts[2];
+  {
     int i = 0;
-    if (R > 0) nts[i++] = R <= 16 * G ? 32 : 64;
-    if (has_shared) nts[i++] = T_shared <= 32 ? 32 : 64;
-    if (part & 1) {
-      int rc = run_gemm_stream(g1, nts, n, act_dtype, status, s);
-      if (rc) return rc;
-    }
-    return (part & 2) ? run_gemm_stream(g2, nts, n, act_dtype, status, s) : MOE_OK;
+    if (R > 0) nts[i++] = row_tile((R + G - 1) / G);
+    if (has_shared) nts[i++] = row_tile(T_shared);
   }
   if (part & 1) {
-    int rc = run_gemm(g1, n, act_dtype, status, s);
+    int rc = stream1 ? run_gemm_stream(g1, nts, n, act_dtype, status, s) : run_gemm(g1, n, act_dtype, status, s);
     if (rc) return rc;
   }
-  return (part & 2) ? run_gemm(g2, n, act_dtype, status, s) : MOE_OK;
+  if (part & 2) return stream2 ? run_gemm_stream(g2, nts, n, act_dtype, status, s) : run_gemm(g2, n, act_dtype, status, s);
+  return MOE_OK;
 }
 
 int moe_expert_ffn_grouped(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets,

@@ -61,12 +61,12 @@ extern "C" {
  * moe_layer_forward) launch:
  *   MOE_FFN_KERNEL_TILED   128 token rows x 256 weight columns per tile
  *                          (prefill-sized groups);
- *   MOE_FFN_KERNEL_STREAM  128 weight rows x 32 or 64 token rows per tile,
- *                          up to 12 stages of weights in flight per SM
- *                          (decode-sized groups: streams the weights);
- *   MOE_FFN_KERNEL_AUTO    (default) STREAM when the routed groups average at
- *                          most 8 rows and the shared expert has at most 96,
- *                          else TILED.
+ *   MOE_FFN_KERNEL_STREAM  one or two blocks of 128 weight rows x a tile of
+ *                          32 to 256 token rows, up to 12 stages of weights
+ *                          in flight per SM (decode-sized groups);
+ *   MOE_FFN_KERNEL_AUTO    (default) STREAM for the gate/up projection when
+ *                          the routed groups average at most 2 rows and the
+ *                          shared expert has at most 32, else TILED.
  * Both kernels give every row the same bits (same k-block order; the tensor
  * cores' result does not depend on operand orientation), so the choice
  * changes speed only. Process-wide; returns the previous choice, or -1 for an

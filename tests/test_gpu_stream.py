@@ -1,9 +1,11 @@
-"""The weight-streaming FFN kernel against the tiled one, through the C ABI.
+"""The FFN kernels against each other, through the C ABI: the
+weight-streaming kernel (one or two interleaved accumulator chains per tile)
+and the tiled kernel.
 
-Both kernels must give every row the same bits: the same products summed over
-the same k-blocks in the same order, with the operands on swapped sides of
-the tensor-core MMA. The comparison is torch.equal on the outputs of the
-public calls with the kernel choice forced each way (moe_set_ffn_kernel),
+Every choice must give every row the same bits: the same products summed over
+the same k-blocks in the same order, whatever the tile shape or the side of
+the tensor-core MMA the operands sit on. The comparison is torch.equal on the
+outputs of the public calls with the kernel choice forced (moe_set_ffn_kernel),
 over decode and prefill-sized batches, bf16 / f16 / int8 weights, the shared
 expert, empty and ragged groups, and N or K not multiples of the tile."""
 
@@ -66,6 +68,7 @@ def _both(fn):
     return a, b
 
 
+
 GEMM_CASES = [
     ([5, 0, 3, 40], 24, 16),  # toy dims, an empty group, N and K below one tile
     ([1, 1, 1, 1, 1, 1], 1408, 2048),  # decode-shaped gate/up
@@ -102,11 +105,12 @@ def c2() -> LayerWeights:
     return LayerWeights(h=2048, i=1408, e=64, i_shared=2816, seed=3)
 
 
-@pytest.mark.parametrize("t", [1, 7, 16, 128, 300, 1024])
+@pytest.mark.parametrize("t", [1, 7, 16, 128, 300, 1024, 4096])
 @pytest.mark.parametrize("quant", [False, True])
 def test_stream_layer_equals_tiled(c2: LayerWeights, t: int, quant: bool) -> None:
     """The whole C2 layer (routed SwiGLU + down + shared expert): the same
-    bits from both kernels, uniform and Zipf routing."""
+    bits from both kernels (the streaming one with one or two chains per
+    tile, depending on the tile count), uniform and Zipf routing."""
     ws = StackedExpertWeights(c2.gate, c2.up, c2.down)
     if quant:
         ws = quantize_stacked_weights(ws, scale_dtype=torch.bfloat16)
