@@ -27,7 +27,7 @@ MOE_ERR_BAD_EXPERT = 6
 MOE_ERR_BAD_OFFSETS = 7
 
 DT_BF16, DT_F16, DT_F32, DT_I8, DT_I32, DT_I64 = range(6)
-FFN_KERNEL_AUTO, FFN_KERNEL_TILED, FFN_KERNEL_STREAM = range(3)
+FFN_KERNEL_AUTO, FFN_KERNEL_TILED, FFN_KERNEL_STREAM, FFN_KERNEL_PAIR = range(4)
 ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
 
 _TORCH_DT = {
@@ -206,9 +206,11 @@ def check_device_status(device: torch.device) -> None:
 
 
 def workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
-    """A zero-initialised byte buffer cached per (device, stream, tag). The
-    grouping kernels need their ticket word zero at first use and leave it
-    zero; caching per stream keeps concurrent streams from sharing it."""
+    """A zero-initialised byte buffer cached per (device, stream, tag), at
+    least ``nbytes`` long. Kernels use it as scratch within one call (the
+    grouping's per-chunk histograms, the router's partial-logit slabs, the
+    FFN's intermediate rows); caching per stream keeps calls on concurrent
+    streams from sharing it."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     key = (idx, stream_ptr(device), tag)
     buf = _workspaces.get(key)

@@ -123,7 +123,11 @@ struct Tile {
   int seg, group, widx, row0, rows, n_tile, split, kb0, kb1;
 };
 
-__device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int t, Tile& tl) {
+// Tile t of the launch -> (segment, group, weight slot, rows, n-tile, K
+// range); rt = token rows per tile. C is the kernel's control block (its
+// seg_tiles, off and mt tables).
+template <class C>
+__device__ __forceinline__ void decode_tile(const C& c, const Params& p, int t, Tile& tl, int rt = BM) {
   int s = 0;
   while (s + 1 < p.num_segs && t >= c.seg_tiles[s]) {
     t -= c.seg_tiles[s];
@@ -152,8 +156,8 @@ __device__ __forceinline__ void decode_tile(const Ctrl& c, const Params& p, int 
   tl.group = lo;
   tl.widx = lo % S.weight_mod;
   tl.n_tile = local / mtg;
-  tl.row0 = c.off[s][lo] + m_tile * BM;
-  tl.rows = min(BM, c.off[s][lo + 1] - tl.row0);
+  tl.row0 = c.off[s][lo] + m_tile * rt;
+  tl.rows = min(rt, c.off[s][lo + 1] - tl.row0);
 }
 
 __device__ __forceinline__ float ld_scale(const void* p, int bf16, int64_t i) {
@@ -273,6 +277,109 @@ __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi
   }
   lo = make_uint4(out[0], out[1], out[2], out[3]);
   hi = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+// Drains one 128-row accumulator into the segment's output: lane i of the
+// calling warp holds tile row r (a row of the tile is valid if r < tl.rows),
+// tb its TMEM address (lane quarter and accumulator columns included); 16-bit
+// rows go out through the warp's 2 KiB staging buffer. Shared by the tiled
+// kernels.
+template <bool kInt8>
+__device__ __forceinline__ void epilogue_rows(const Params& p, const Segment& Sg, const Tile& tl, uint32_t tb,
+                                              int r, int lane, uint4* estage) {
+  bool valid = r < tl.rows;
+  void* obase = Sg.out;
+  int64_t orow = tl.row0 + r;
+  if (Sg.out_rows && valid) {
+    const int code = Sg.out_rows[orow];
+    const int dst = code & 15;
+    orow = code >> 4;
+    if (code < 0 || dst >= Sg.out_table_n || orow >= Sg.out_table_rows) {
+      if (p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
+      valid = false;
+    } else {
+      obase = Sg.out_table[dst];
+    }
+  }
+  const int64_t row_off = orow * Sg.ldo + tl.split * Sg.split_stride;
+  const bool vec_ok = (Sg.ldo % 8) == 0;
+  const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
+  const int oc = out_cols_per_tile(Sg);
+  const int n0 = tl.n_tile * oc;
+  // whole 32-column chunks of 16-bit rows go through the staged store
+  const bool staged = !Sg.out_f32 && vec_ok && (Sg.n % 32) == 0;
+  uint16_t* rowp[4];
+  {
+    uint16_t* mine = valid ? reinterpret_cast<uint16_t*>(obase) + row_off : nullptr;
+#pragma unroll
+    for (int s2 = 0; s2 < 4; ++s2)
+      rowp[s2] = reinterpret_cast<uint16_t*>(
+          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(mine), s2 * 8 + (lane >> 2)));
+  }
+  if (Sg.swiglu) {
+#pragma unroll 1
+    for (int ch = 0; ch < oc / 32; ++ch) {
+      uint32_t gv[32], uv[32];
+      tmem_ld_32x32b_x32(tb + ch * 32, gv);
+      tmem_ld_32x32b_x32(tb + oc + ch * 32, uv);
+      tmem_ld_wait();
+      const int col0 = n0 + ch * 32;
+      if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
+        const int nc = min(32, Sg.n - col0);
+        float h[32];
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float gs[8], us[8];
+          if (kInt8 && Sg.b_int8) {
+            ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, gs);
+            ld_scales8(Sg.scale1, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, us);
+          }
+#pragma unroll
+          for (int j8 = 0; j8 < 8; ++j8) {
+            const int j = 8 * q8 + j8;
+            float g = __uint_as_float(gv[j]);
+            float u = __uint_as_float(uv[j]);
+            if (kInt8 && Sg.b_int8 && j < nc) {
+              g *= gs[j8];
+              u *= us[j8];
+            }
+            h[j] = g / (1.0f + __expf(-g)) * u;
+          }
+        }
+        if (staged)
+          store_block32_staged(estage, h, p.in_f16, lane, rowp, col0);
+        else
+          store_row32(obase, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int ch = 0; ch < oc / 32; ++ch) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tb + ch * 32, v);
+      tmem_ld_wait();
+      const int col0 = n0 + ch * 32;
+      if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
+        const int nc = min(32, Sg.n - col0);
+        float o[32];
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float ss[8];
+          if (kInt8 && Sg.b_int8) ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, ss);
+#pragma unroll
+          for (int j8 = 0; j8 < 8; ++j8) {
+            const int j = 8 * q8 + j8;
+            o[j] = __uint_as_float(v[j]);
+            if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ss[j8];
+          }
+        }
+        if (staged)
+          store_block32_staged(estage, o, p.in_f16, lane, rowp, col0);
+        else
+          store_row32(obase, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
+      }
+    }
+  }
 }
 
 template <bool kInt8>
@@ -533,99 +640,7 @@ __global__ void __launch_bounds__(Config<kInt8>::kThreads)
       if (!wait_parity_bounded(&c.tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      bool valid = r < tl.rows;
-      void* obase = Sg.out;
-      int64_t orow = tl.row0 + r;
-      if (Sg.out_rows && valid) {
-        const int code = Sg.out_rows[orow];
-        const int dst = code & 15;
-        orow = code >> 4;
-        if (code < 0 || dst >= Sg.out_table_n || orow >= Sg.out_table_rows) {
-          if (p.status) atomicCAS(p.status, 0, MOE_ERR_BAD_OFFSETS);
-          valid = false;
-        } else {
-          obase = Sg.out_table[dst];
-        }
-      }
-      const int64_t row_off = orow * Sg.ldo + tl.split * Sg.split_stride;
-      const bool vec_ok = (Sg.ldo % 8) == 0;
-      const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
-      const int oc = out_cols_per_tile(Sg);
-      const int n0 = tl.n_tile * oc;
-      // whole 32-column chunks of 16-bit rows go through the staged store
-      const bool staged = !Sg.out_f32 && vec_ok && (Sg.n % 32) == 0;
-      uint16_t* rowp[4];
-      {
-        uint16_t* mine = valid ? reinterpret_cast<uint16_t*>(obase) + row_off : nullptr;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2)
-          rowp[s2] = reinterpret_cast<uint16_t*>(
-              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(mine), s2 * 8 + (lane >> 2)));
-      }
-      if (Sg.swiglu) {
-#pragma unroll 1
-        for (int ch = 0; ch < oc / 32; ++ch) {
-          uint32_t gv[32], uv[32];
-          tmem_ld_32x32b_x32(tb + ch * 32, gv);
-          tmem_ld_32x32b_x32(tb + oc + ch * 32, uv);
-          tmem_ld_wait();
-          const int col0 = n0 + ch * 32;
-          if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
-            const int nc = min(32, Sg.n - col0);
-            float h[32];
-#pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-              float gs[8], us[8];
-              if (kInt8 && Sg.b_int8) {
-                ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, gs);
-                ld_scales8(Sg.scale1, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, us);
-              }
-#pragma unroll
-              for (int j8 = 0; j8 < 8; ++j8) {
-                const int j = 8 * q8 + j8;
-                float g = __uint_as_float(gv[j]);
-                float u = __uint_as_float(uv[j]);
-                if (kInt8 && Sg.b_int8 && j < nc) {
-                  g *= gs[j8];
-                  u *= us[j8];
-                }
-                h[j] = g / (1.0f + __expf(-g)) * u;
-              }
-            }
-            if (staged)
-              store_block32_staged(estage, h, p.in_f16, lane, rowp, col0);
-            else
-              store_row32(obase, row_off + col0, h, nc, p.in_f16, 0, vec_ok);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int ch = 0; ch < oc / 32; ++ch) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tb + ch * 32, v);
-          tmem_ld_wait();
-          const int col0 = n0 + ch * 32;
-          if (staged ? col0 < Sg.n : (valid && col0 < Sg.n)) {
-            const int nc = min(32, Sg.n - col0);
-            float o[32];
-#pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-              float ss[8];
-              if (kInt8 && Sg.b_int8) ld_scales8(Sg.scale0, Sg.scale_bf16, sc_base + col0 + 8 * q8, nc - 8 * q8, ss);
-#pragma unroll
-              for (int j8 = 0; j8 < 8; ++j8) {
-                const int j = 8 * q8 + j8;
-                o[j] = __uint_as_float(v[j]);
-                if (kInt8 && Sg.b_int8 && j < nc) o[j] *= ss[j8];
-              }
-            }
-            if (staged)
-              store_block32_staged(estage, o, p.in_f16, lane, rowp, col0);
-            else
-              store_row32(obase, row_off + col0, o, nc, p.in_f16, Sg.out_f32, Sg.out_f32 ? (Sg.ldo % 4) == 0 : vec_ok);
-          }
-        }
-      }
+      epilogue_rows<kInt8>(p, Sg, tl, tb, r, lane, estage);
       tc_fence_before();
       mbar_arrive(&c.tempty[acc]);
       acc ^= 1u;

@@ -17,6 +17,7 @@
 #include "combine.cuh"
 #include "ep.cuh"
 #include "gemm.cuh"
+#include "gemm2sm.cuh"
 #include "gemm_stream.cuh"
 #include "group.cuh"
 #include "route.cuh"
@@ -191,6 +192,9 @@ struct SegSpec {
   // rows of the A (activation) TMA box: 128 for the tiled kernel, the row
   // tile for the streaming kernel
   int a_box_rows = moe::gemm::BM;
+  // rows of the weight TMA boxes; 0: mma_n (mma_n / 2 for SwiGLU). The CTA-pair
+  // kernel loads 128 weight rows per CTA.
+  int b_box_rows = 0;
 };
 
 int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
@@ -199,7 +203,7 @@ int fill_segment(moe::gemm::Segment* s, const SegSpec& sp, int act_dtype) {
   int rc = sp.gather_rows ? make_map_a(&s->map_a, sp.a, act_dtype, sp.gather_src_rows, sp.K, sp.lda, 1)
                           : make_map_a(&s->map_a, sp.a, act_dtype, sp.a_rows, sp.K, sp.lda, sp.a_box_rows);
   if (rc) return rc;
-  const int box_rows = sp.swiglu ? sp.mma_n / 2 : sp.mma_n;
+  const int box_rows = sp.b_box_rows > 0 ? sp.b_box_rows : (sp.swiglu ? sp.mma_n / 2 : sp.mma_n);
   const int64_t gw = sp.Gw > 0 ? sp.Gw : sp.G;
   rc = make_map_b(&s->map_b0, sp.b0, sp.b_dtype, gw, sp.N, sp.K, box_rows);
   if (rc) return rc;
@@ -329,6 +333,70 @@ int run_gemm(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, 
   return any_i8 ? launch_gemm<true>(p, grid, stream) : launch_gemm<false>(p, grid, stream);
 }
 
+// ---------------------------------------------------------------- CTA-pair kernel
+// Cluster launch of two CTAs per tile (programmatic dependent launch too).
+int launch_pair(const moe::gemm::Params& p, int grid, cudaStream_t stream) {
+  constexpr size_t smem = moe::gemm::pair_smem_bytes();
+  static_assert(smem <= 232448, "shared memory of the CTA-pair kernel");
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(pair gemm)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(moe::gemm::kPairThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  CUDA_TRY(cudaLaunchKernelEx(&cfg, moe::gemm::grouped_gemm_pair_kernel, p), "grouped_gemm_pair_kernel launch");
+  return MOE_OK;
+}
+
+// The CTA-pair kernel over up to two FFN segments (16-bit weights, one K
+// range, no gathered rows, 16-bit outputs): tiles of 256 rows x 256 columns.
+int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  moe::gemm::Params p;
+  std::memset(&p, 0, sizeof(p));
+  int64_t tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    SegSpec spec = specs_in[i];
+    CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
+              "the CTA-pair kernel takes 16-bit weights, one K range, 16-bit outputs");
+    spec.mma_n = 2 * moe::gemm::BM;
+    spec.b_box_rows = moe::gemm::BM;  // each CTA loads 128 weight rows
+    rc = check_seg(spec, act_dtype);
+    if (rc) return rc;
+    rc = fill_segment(&p.seg[i], spec, act_dtype);
+    if (rc) return rc;
+    const int oc = spec.swiglu ? moe::gemm::BM : 2 * moe::gemm::BM;
+    const int64_t rt = 2 * moe::gemm::BM;
+    const int64_t mt = spec.offsets ? spec.a_rows / rt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
+                                    : (spec.a_rows + rt - 1) / rt;
+    tiles += mt * ((spec.N + oc - 1) / oc);
+    p.remote_out |= spec.out_rows ? 1 : 0;
+  }
+  p.num_segs = nseg;
+  p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
+  p.status = status;
+  const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
+  if (pairs <= 0) return MOE_OK;
+  return launch_pair(p, static_cast<int>(2 * pairs), stream);
+}
+
 // ---------------------------------------------------------------- streaming kernel
 std::atomic<int> g_ffn_kernel{MOE_FFN_KERNEL_AUTO};
 
@@ -453,7 +521,9 @@ extern "C" {
 int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
 
 int moe_set_ffn_kernel(int choice) {
-  if (choice != MOE_FFN_KERNEL_AUTO && choice != MOE_FFN_KERNEL_TILED && choice != MOE_FFN_KERNEL_STREAM) return -1;
+  if (choice != MOE_FFN_KERNEL_AUTO && choice != MOE_FFN_KERNEL_TILED && choice != MOE_FFN_KERNEL_STREAM &&
+      choice != MOE_FFN_KERNEL_PAIR)
+    return -1;
   return g_ffn_kernel.exchange(choice);
 }
 
@@ -859,11 +929,37 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     if (R > 0) nts[i++] = row_tile((R + G - 1) / G);
     if (has_shared) nts[i++] = row_tile(T_shared);
   }
+  // The CTA-pair kernel (16-bit weights) when its 256-row tiles compute no
+  // more rows than the tiled kernel's 128-row tiles (within 5%), judged from
+  // the average group: both kernels ran at about the same tensor rate per
+  // computed row on B200, the pair kernel some 5-13% faster (C2 gate/up:
+  // T=2048 237 -> 210 us, both computing 256 rows for groups of ~192), so the
+  // rows a tile shape wastes decide (T=4096, groups of ~384: 376 vs 405 us).
+  const bool pairable = streamable && w_dtype != MOE_DT_I8;
+  CHECK_ARG(choice != MOE_FFN_KERNEL_PAIR || pairable, "the CTA-pair kernel takes 16-bit weights and no gathered rows");
+  auto rounded = [](int64_t rows, int64_t tile) { return (rows + tile - 1) / tile * tile; };
+  int64_t rows128 = 0, rows256 = 0;  // rows computed by 128- and 256-row tiles
+  if (R > 0) {
+    const int64_t avg = (R + G - 1) / G;
+    rows128 += G * rounded(avg, 128);
+    rows256 += G * rounded(avg, 256);
+  }
+  if (has_shared) {
+    rows128 += rounded(T_shared, 128);
+    rows256 += rounded(T_shared, 256);
+  }
+  const bool pair = choice == MOE_FFN_KERNEL_PAIR ||
+                    (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && rows256 * 20 <= rows128 * 21);
+  auto launch = [&](const SegSpec* g, bool stream_it) {
+    if (stream_it) return run_gemm_stream(g, nts, n, act_dtype, status, s);
+    if (pair) return run_gemm_pair(g, n, act_dtype, status, s);
+    return run_gemm(g, n, act_dtype, status, s);
+  };
   if (part & 1) {
-    int rc = stream1 ? run_gemm_stream(g1, nts, n, act_dtype, status, s) : run_gemm(g1, n, act_dtype, status, s);
+    int rc = launch(g1, stream1);
     if (rc) return rc;
   }
-  if (part & 2) return stream2 ? run_gemm_stream(g2, nts, n, act_dtype, status, s) : run_gemm(g2, n, act_dtype, status, s);
+  if (part & 2) return launch(g2, stream2);
   return MOE_OK;
 }
 

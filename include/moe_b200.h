@@ -61,21 +61,27 @@ extern "C" {
  * moe_layer_forward) launch:
  *   MOE_FFN_KERNEL_TILED   128 token rows x 256 weight columns per tile
  *                          (prefill-sized groups);
+ *   MOE_FFN_KERNEL_PAIR    256 token rows x 256 weight columns per tile on a
+ *                          pair of SMs (tcgen05 cta_group::2, each SM stages
+ *                          half of both operands); 16-bit weights only;
  *   MOE_FFN_KERNEL_STREAM  one or two blocks of 128 weight rows x a tile of
  *                          32 to 256 token rows, up to 12 stages of weights
  *                          in flight per SM (decode-sized groups);
  *   MOE_FFN_KERNEL_AUTO    (default) STREAM for the gate/up projection when
  *                          the routed groups average at most 2 rows and the
- *                          shared expert has at most 32, else TILED.
- * Both kernels give every row the same bits (same k-block order; the tensor
- * cores' result does not depend on operand orientation), so the choice
- * changes speed only. Process-wide; returns the previous choice, or -1 for an
+ *                          shared expert has at most 32; else PAIR when its
+ *                          256-row tiles compute no more rows than 128-row
+ *                          tiles would (16-bit weights), else TILED.
+ * Every kernel gives every row the same bits (same k-block order; the tensor
+ * cores' result depends neither on operand orientation nor on the tile or
+ * CTA-group shape), so the choice changes speed only. Process-wide; returns the previous choice, or -1 for an
  * unknown one (nothing changes). No reference counterpart: the reference's
  * tile size is the caller's block_m (src/dispatch/kernels/tile_schedule.py).
  */
 #define MOE_FFN_KERNEL_AUTO 0
 #define MOE_FFN_KERNEL_TILED 1
 #define MOE_FFN_KERNEL_STREAM 2
+#define MOE_FFN_KERNEL_PAIR 3
 int moe_set_ffn_kernel(int choice);
 
 /* router modes */

@@ -132,3 +132,39 @@ def test_stream_is_the_automatic_choice_for_decode(c2: LayerWeights) -> None:
         auto = fwd()
     a, b = _both(fwd)
     assert torch.equal(auto, a) and torch.equal(auto, b)
+
+
+def _pair_vs_tiled(fn):
+    with ffn_kernel(L.FFN_KERNEL_TILED):
+        a = fn()
+    with ffn_kernel(L.FFN_KERNEL_PAIR):
+        b = fn()
+    torch.cuda.synchronize()
+    return a, b
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("sizes", "n", "k"), GEMM_CASES)
+def test_pair_grouped_matmul_equals_tiled(dtype, sizes, n, k) -> None:
+    """The CTA-pair kernel (256-row tiles over two SMs, cta_group::2) gives
+    the tiled kernel's bits on plain GEMMs: empty groups, groups of a few rows
+    (the pair's second half holding other groups' rows or nothing), N and K
+    not multiples of the tile."""
+    g = torch.Generator(device="cuda").manual_seed(33)
+    sched = build_tile_schedule(torch.tensor(sizes, device=DEV), block_m=16)
+    x = randn((sum(sizes), k), g, 1.0, dtype)
+    w = randn((len(sizes), n, k), g, k ** -0.5, dtype)
+    a, b = _pair_vs_tiled(lambda: grouped_matmul(x, w, sched))
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("t", [1, 300, 1024, 4096])
+def test_pair_layer_equals_tiled(c2: LayerWeights, t: int) -> None:
+    """The whole C2 layer (SwiGLU with gate and up on the two SMs of a pair,
+    down, shared expert): the CTA-pair kernel gives the tiled kernel's bits."""
+    ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
+    x = randn((t, 2048), torch.Generator(device="cuda").manual_seed(950 + t), 1.0)
+    for bias in (None, -1.2 * torch.log(torch.arange(64, dtype=torch.float32, device=DEV) + 1.0)):
+        a, b = _pair_vs_tiled(lambda: moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6), shared=sh,
+                                                        e_score_bias=bias).out)
+        assert torch.equal(a, b), f"T={t}: max |diff| {(a.float() - b.float()).abs().max().item()}"
