@@ -448,6 +448,37 @@ def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
     return start.elapsed_time(end) / steps
 
 
+def host_copy_ceiling(x_host, out_host, dev, world: int, n: int = 20) -> float:
+    """The host link's ceiling for the e2e number: one step's input copy
+    (host -> device) and output copy (device -> host) from the same pinned
+    buffers, on the copy streams run_host_batches uses, with every rank
+    copying at once; returns steps/s (max time over ranks)."""
+    import torch
+
+    xd = torch.empty(x_host.shape, dtype=x_host.dtype, device=dev)
+    od = torch.zeros(out_host.shape, dtype=out_host.dtype, device=dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    cur = torch.cuda.current_stream(dev)
+    start.record(cur)
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    for _ in range(n):
+        with torch.cuda.stream(h2d):
+            xd.copy_(x_host, non_blocking=True)
+        with torch.cuda.stream(d2h):
+            out_host.copy_(od, non_blocking=True)
+    cur.wait_stream(h2d)
+    cur.wait_stream(d2h)
+    end.record(cur)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / n, world)
+    barrier(world)
+    return 1e3 / ms
+
+
 def run_b200(args, wl: Workload) -> None:
     import torch
 
@@ -468,6 +499,21 @@ def run_b200(args, wl: Workload) -> None:
         bias = (-1.2 * torch.log(torch.arange(wl.E, dtype=torch.float32, device=dev) + 1.0))
 
     ep = None
+    if args.profile_ep_sim:
+        # profiler driver for the EP kernels on one GPU: W ranks emulated as
+        # buffers on this device (dispatch, FFN with return stores, combine)
+        if world > 1:
+            raise SystemExit("--profile-ep-sim runs on one GPU")
+        from dispatch_b200.kernels.ep_sim import simulated_ep_forward
+
+        xs = [x] + [torch.randn(t, wl.H, generator=torch.Generator(device=dev).manual_seed(1000 * r), device=dev)
+                    .to(torch.bfloat16) for r in range(1, args.profile_ep_sim)]
+        for _ in range(max(args.profile_calls, 1)):
+            simulated_ep_forward(xs, router, ws, sh, cfg, bias, check_offsets=False)
+        torch.cuda.synchronize()
+        L.check_device_status(dev)
+        print(f"profile-ep-sim ok: {args.profile_ep_sim} ranks x {wl.name} T={t}", flush=True)
+        return
     if args.profile_calls:
         # profiler driver: the bare layer call, no timing and no JSON line
         if world > 1:
@@ -483,7 +529,8 @@ def run_b200(args, wl: Workload) -> None:
         if args.ep_transport == "peer":
             from dispatch_b200.kernels.ep_peer import PeerEPLayer
 
-            ep = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t)
+            ep = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t,
+                             chunks=args.ep_chunks)
         else:
             from dispatch_b200.kernels.expert_parallel import EPLayer
 
@@ -493,7 +540,8 @@ def run_b200(args, wl: Workload) -> None:
             return ep(xx)
 
         launches_per_step = ep.launches_for(t) if hasattr(ep, "launches_for") else ep.launches_per_step
-        parallelism = f"ep{world} ({args.ep_transport})"
+        parallelism = f"ep{world} ({args.ep_transport}" + (f", {args.ep_chunks} chunks)" if args.ep_chunks > 1 and
+                                                           args.ep_transport == "peer" else ")")
     else:
         def layer(xx):
             return moe_layer_forward(xx, router, ws, cfg, shared=sh, e_score_bias=bias).out
@@ -540,6 +588,7 @@ def run_b200(args, wl: Workload) -> None:
         time_loop(lambda: run_host_batches(layer, [x_host] * n_e2e, [out_host] * n_e2e), 1, 1, world, stream),
         world) / n_e2e
     e2e_val = t * world / (e2e_ms * 1e-3)
+    copy_steps_per_s = host_copy_ceiling(x_host, out_host, dev, world)
 
     # expert-parallel phase split: CUDA events between the phases of a call,
     # mean over calls, max over ranks (names the limiter of the N-GPU step)
@@ -609,7 +658,10 @@ def run_b200(args, wl: Workload) -> None:
             "layer_tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
             "roofline": roof,
             "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s", "h2d_bytes_per_step": t * wl.H * 2,
-                    "d2h_bytes_per_step": t * wl.H * 2},
+                    "d2h_bytes_per_step": t * wl.H * 2,
+                    # the copies alone, every rank at once: the host link's ceiling on e2e
+                    "host_copy_ceiling": round(copy_steps_per_s * t * world, 1),
+                    "host_copy_gbs_per_gpu": round(copy_steps_per_s * 2 * t * wl.H * 2 / 1e9, 1)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "sweep": sweep,
@@ -695,8 +747,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: NVLink peer stores fused into dispatch/FFN (peer) or NCCL all-to-all (nccl)")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="N>1, peer transport: split each call's tokens into this many chunks on their own streams "
+                         "so one chunk's dispatch overlaps the previous chunk's FFN")
     ap.add_argument("--profile-calls", type=int, default=0,
                     help="run the layer this many times and exit (a driver for ncu launch lists and captures)")
+    ap.add_argument("--profile-ep-sim", type=int, default=0, metavar="W",
+                    help="run the expert-parallel layer with W ranks emulated on one GPU (--profile-calls times) "
+                         "and exit: a one-GPU driver for ncu captures of the EP kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -155,7 +155,7 @@ class PeerEPLayer:
                  e_score_bias=None, n_experts: int | None = None, weights_are_local: bool = False,
                  max_tokens: int = 4096, act_dtype: torch.dtype = torch.bfloat16,
                  buffers: PeerBuffers | None = None, overlap_shared: bool = False,
-                 overlap_min_tokens: int = 1024):
+                 overlap_min_tokens: int = 1024, chunks: int = 1, chunk_min_tokens: int = 1024):
         from dispatch_b200.kernels.expert_parallel import _slice_experts  # noqa: PLC0415
         from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights  # noqa: PLC0415
 
@@ -185,13 +185,32 @@ class PeerEPLayer:
         # of at least overlap_min_tokens tokens split it off. Off by default:
         # at 8 GPUs the step was slower with it (0.92 ms), the shared GEMM's
         # persistent CTAs leaving one dispatch CTA per SM for 7x more rows.
-        self.overlap_shared = overlap_shared and shared is not None
+        self.overlap_shared = overlap_shared and shared is not None and chunks == 1
         self.overlap_min_tokens = overlap_min_tokens
         self._side: torch.cuda.Stream | None = None
+        # Chunked calls: a call of at least chunk_min_tokens tokens is split
+        # into `chunks` row ranges, each run through its own peer buffers on
+        # its own stream, so chunk c+1's routing, count exchange and NVLink
+        # dispatch run while chunk c's FFN has the tensor cores (the small
+        # dispatch and exchange CTAs fit beside the FFN's persistent CTA on
+        # each SM). Rows are independent and the router is batch-invariant, so
+        # the output is the same bits as one unchunked call. Chunk 0 uses
+        # `buffers` (sized for max_tokens); the others get buffers sized for
+        # ceil(max_tokens / chunks).
+        if chunks < 1:
+            raise ValueError(f"chunks={chunks} must be >= 1")
+        self.chunks, self.chunk_min_tokens = chunks, chunk_min_tokens
+        self._chunk_bufs = [
+            PeerBuffers(rank=rank, world=world, group=group, device=g.device,
+                        max_tokens=(max_tokens + chunks - 1) // chunks, top_k=self.top_k, hidden=self.hidden,
+                        n_experts=e, act_dtype=self.act_dtype)
+            for _ in range(chunks - 1)]
+        self._chunk_streams = [torch.cuda.Stream(g.device) for _ in range(chunks - 1)]
         # launches of this library per call: route x2, group x2, exchange x3, dispatch, FFN x2 (+2 shared), combine
         self.launches_per_step = 13 if self.overlap_shared else 11
         # Set to a list to have each call append (phase name, CUDA event)
-        # marks, recorded on the current stream after each phase.
+        # marks, recorded on the current stream after each phase (of the first
+        # chunk, in a chunked call).
         self.phase_events: list | None = None
 
     PHASES = ("route_group", "count_exchange", "dispatch", "barrier_after_dispatch", "ffn_and_return",
@@ -205,9 +224,15 @@ class PeerEPLayer:
 
     def launches_for(self, t: int) -> int:
         """Launches of this library in one call on t tokens."""
+        if self.chunks > 1 and t >= self.chunk_min_tokens:
+            return 11 * self.chunks
         return 13 if (self.overlap_shared and t >= self.overlap_min_tokens) else 11
 
     def close(self) -> None:
+        """Collective: frees the peer buffers (every rank calls it)."""
+        for b in self._chunk_bufs:
+            b.close()
+        self._chunk_bufs = []
         if self._own_buffers:
             self.buf.close()
 
@@ -231,25 +256,55 @@ class PeerEPLayer:
 
     @torch.no_grad()
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        dev = L.require_cuda(x, what="expert-parallel layer")
+        t, h = x.shape
+        if t > self.buf.max_tokens:
+            raise ValueError(f"{t} tokens exceed the {self.buf.max_tokens} tokens per rank the peer buffers hold")
+        if h != self.hidden or x.dtype != self.buf.act_dtype:
+            raise ValueError(f"x must be ({t}, {self.hidden}) {self.buf.act_dtype}, got {tuple(x.shape)} {x.dtype}")
+        x = x.contiguous()
+        out = torch.empty(t, h, dtype=x.dtype, device=dev)
+        if self.chunks == 1 or t < self.chunk_min_tokens:
+            self._forward(x, out, self.buf, dev, mark=True)
+            return out
+        # every rank splits the same way and makes the same exchange calls on
+        # each chunk's buffers, in the same order
+        bounds = [t * c // self.chunks for c in range(self.chunks + 1)]
+        main = torch.cuda.current_stream(dev)
+        for c in range(self.chunks):
+            lo, hi = bounds[c], bounds[c + 1]
+            if c == 0:
+                self._forward(x[lo:hi], out[lo:hi], self.buf, dev, mark=True)
+                continue
+            s = self._chunk_streams[c - 1]
+            s.wait_stream(main)
+            with torch.cuda.stream(s):
+                self._forward(x[lo:hi], out[lo:hi], self._chunk_bufs[c - 1], dev, mark=False)
+            x.record_stream(s)
+            out.record_stream(s)
+        for s in self._chunk_streams:
+            main.wait_stream(s)
+        return out
+
+    def _forward(self, x: torch.Tensor, out: torch.Tensor, buf: PeerBuffers, dev: torch.device, *,
+                 mark: bool) -> None:
+        """One pass of the EP round trip for x (rows of this rank) through
+        `buf`, on the current stream; the combined rows go to `out`."""
         from dispatch_b200.kernels.grouping import _group  # noqa: PLC0415
         from dispatch_b200.kernels.layer import route  # noqa: PLC0415
 
-        dev = L.require_cuda(x, what="expert-parallel layer")
         t, h = x.shape
-        buf = self.buf
         if t > buf.max_tokens:
             raise ValueError(f"{t} tokens exceed the {buf.max_tokens} tokens per rank the peer buffers hold")
-        if h != self.hidden or x.dtype != buf.act_dtype:
-            raise ValueError(f"x must be ({t}, {self.hidden}) {buf.act_dtype}, got {tuple(x.shape)} {x.dtype}")
-        x = x.contiguous()
+        mark_fn = self._mark if mark else (lambda name: None)
         lib = L.lib()
         st = L.status_word(dev).data_ptr()
         stream = L.stream_ptr(dev)
         k = self.top_k
-        self._mark("start")
+        mark_fn("start")
         idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
         counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
-        self._mark("route_group")
+        mark_fn("route_group")
         sh = self.shared
         i_sh = 0 if sh is None else sh.gate.shape[0]
         ys = torch.empty(t, h, dtype=x.dtype, device=dev) if sh is not None else None
@@ -269,16 +324,16 @@ class PeerEPLayer:
         buf.epoch += 1
         epoch = buf.epoch
         buf.exchange(counts, 0, epoch)
-        self._mark("count_exchange")
+        mark_fn("count_exchange")
         rc = lib.moe_ep_dispatch(
             x.data_ptr(), L.dt(x), t, h, idx.data_ptr(), L.dt(idx), k, pos.data_ptr(), offsets.data_ptr(),
             buf.counts_all_ptr, self.rank, self.world, self.n_experts, buf.t_recv.data_ptr(),
             buf.t_ret.data_ptr(), buf.recv_cap, buf.recv_offsets.data_ptr(), st, stream,
         )
         L.check(rc, "moe_ep_dispatch")
-        self._mark("dispatch")
+        mark_fn("dispatch")
         buf.exchange(None, 1, epoch)
-        self._mark("barrier_after_dispatch")
+        mark_fn("barrier_after_dispatch")
         fused_shared = sh is not None and not overlap
         wq = self.weights
         g, u, d = (wq.gate.data, wq.up.data, wq.down.data) if self.quant else (wq.gate, wq.up, wq.down)
@@ -296,14 +351,12 @@ class PeerEPLayer:
             ws.numel(), st, stream,
         )
         L.check(rc, "moe_ep_expert_ffn")
-        self._mark("ffn_and_return")
+        mark_fn("ffn_and_return")
         buf.exchange(None, 2, epoch)
-        self._mark("barrier_after_ffn")
+        mark_fn("barrier_after_ffn")
         if shared_done is not None:
             torch.cuda.current_stream(dev).wait_event(shared_done)
-        out = torch.empty(t, h, dtype=x.dtype, device=dev)
         rc = lib.moe_combine(buf.back_ptr, L.dt(x), pos.data_ptr(), wf.data_ptr(), t, k, h, L.ptr(ys),
                              out.data_ptr(), L.dt(out), st, stream)
         L.check(rc, "moe_combine")
-        self._mark("combine")
-        return out
+        mark_fn("combine")
