@@ -429,6 +429,36 @@ def check_layer_output(x, out, router, ws, sh, cfg, bias, n_rows: int = 64) -> d
     return {"rows": int(rows.numel()), "max_abs_err": round(float((got - ref).abs().max()), 5), "bar": bar}
 
 
+def router_id_agreement(x, router, cfg, bias) -> dict:
+    """Router ids of the route kernels (tensor-core f32 logits, fused
+    selection) against a float64 torch selection from float64 logits on the
+    same tokens: the fraction of (token, slot) ids in the float64 top-k set,
+    and of tokens whose whole top-k set matches. Ids can only differ where two
+    experts' scores tie to within the f32 logits' rounding."""
+    import torch
+
+    from dispatch_b200.kernels.layer import route
+
+    idx, _ = route(x, router, cfg, e_score_bias=bias)
+    lg = x.double() @ router.double().T
+    b = 0.0 if bias is None else bias.double()
+    if cfg.mode == "softmax":
+        s = lg + b
+    else:  # group-limited sigmoid: select on sigmoid + bias within the best groups
+        s = torch.sigmoid(lg) + b
+        t, e = s.shape
+        per = e // cfg.n_group
+        gsc = s.view(t, cfg.n_group, per).topk(2, dim=-1).values.sum(-1)
+        keep = torch.zeros_like(gsc, dtype=torch.bool).scatter_(1, gsc.topk(cfg.topk_group, dim=-1).indices, True)
+        s = s.masked_fill(~keep.repeat_interleave(per, 1), float("-inf"))
+    ref = s.topk(cfg.top_k, dim=-1).indices
+    got = idx.long()
+    hits = (got[:, :, None] == ref[:, None, :]).any(-1)
+    return {"tokens": int(got.shape[0]), "slot_agreement": round(float(hits.float().mean()), 6),
+            "token_set_agreement": round(float(hits.all(-1).float().mean()), 6),
+            "vs": "float64 torch selection from float64 logits"}
+
+
 def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
     import torch
 
@@ -571,6 +601,9 @@ def run_b200(args, wl: Workload) -> None:
             dist.destroy_process_group()
         raise SystemExit(1)
 
+    router_ids = router_id_agreement(x, router, cfg, bias)
+    torch.cuda.synchronize()
+
     with ClockSampler(local) as clocks:
         ms = time_loop(lambda: layer(x), args.steps, args.warmup, world, stream)
     ms = max_over_ranks(ms, world)
@@ -642,6 +675,12 @@ def run_b200(args, wl: Workload) -> None:
                          "tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
                          "tensor_frac": round(wl.flops(t) / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
 
+    # the same layer with int8 routed experts (C3), so one bench line also
+    # measures the int8 GEMM path at the bench's token count
+    int8_layer = None
+    if world == 1 and not args.no_sweep and not wl.int8:
+        int8_layer = int8_layer_line(t, peaks, dev, stream)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -655,6 +694,7 @@ def run_b200(args, wl: Workload) -> None:
                        "routed_weight_bytes": weight_footprint(ws),
                        "l2": "inputs larger than L2 (expert weights >= 1.1 GB per step)"},
             "checked": checked,
+            "router_ids": router_ids,
             "layer_tflops_algorithmic": round(wl.flops(t) / (ms * 1e-3) / 1e12, 1),
             "roofline": roof,
             "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s", "h2d_bytes_per_step": t * wl.H * 2,
@@ -665,6 +705,7 @@ def run_b200(args, wl: Workload) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "sweep": sweep,
+            "int8_layer": int8_layer,
             "ep_phases_ms": ep_phases,
             "peaks": {"kind": peak_kind, "hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"]},
         }
@@ -677,6 +718,34 @@ def run_b200(args, wl: Workload) -> None:
         if hasattr(ep, "close"):
             ep.close()
         dist.destroy_process_group()
+
+
+def int8_layer_line(t: int, peaks: dict, dev, stream) -> dict:
+    """C3 at T tokens (routed experts int8 with bf16 per-channel scales,
+    shared expert bf16): output checked against f32 on the dequantised
+    weights (refused, and not timed, if it disagrees), then the step timed as
+    a CUDA graph (device time, inputs larger than L2)."""
+    import torch
+
+    from dispatch_b200.kernels.layer import CapturedLayer, RouterConfig, moe_layer_forward
+
+    w3 = WORKLOADS["c3"]
+    x, router, ws, sh, bias = make_inputs(w3, t, seed=0, dev=dev)
+    cfg = RouterConfig(top_k=w3.k, mode=w3.router, renormalize=w3.renorm, n_group=w3.n_group,
+                       topk_group=w3.topk_group, routed_scaling_factor=w3.scaling)
+    out = moe_layer_forward(x, router, ws, cfg, shared=sh, e_score_bias=bias).out
+    torch.cuda.synchronize()
+    try:
+        checked = check_layer_output(x, out, router, ws, sh, cfg, bias)
+    except AssertionError as exc:
+        return {"workload": f"{w3.desc}, T={t}", "refused": str(exc).splitlines()[0][:300]}
+    cap = CapturedLayer(x, router, ws, cfg, shared=sh, e_score_bias=bias)
+    ms = time_loop(cap.replay, 50, 5, 1, stream)
+    del cap
+    tf = w3.flops(t) / (ms * 1e-3) / 1e12
+    return {"workload": f"{w3.desc}, T={t}", "graph_ms": round(ms, 4), "tokens_per_s": round(t / (ms * 1e-3), 1),
+            "tflops_algorithmic": round(tf, 1), "tensor_frac": round(tf / peaks["bf16_tflops"], 4),
+            "checked": checked}
 
 
 # DRAM bytes (read + write) of one gate/up launch on the C2 T=4096 step, from

@@ -14,10 +14,11 @@
 // weight, and the epilogue writes h = silu(gate) * up; in a plain segment all
 // mma_n columns are outputs (bf16/f16, or f32 for the router logits).
 //
-// Warp roles (256 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
-// issues tcgen05.mma from one thread, warps 2-3 dequantise int8 weight tiles to
-// bf16/f16 in shared memory (int8 build only), warps 4-7 drain the
-// double-buffered TMEM accumulator (lane quarter = warp % 4) and store.
+// Warp roles: warp 0 issues TMA loads, warp 1 owns TMEM and issues
+// tcgen05.mma from one thread, then (int8 build only) ten warps dequantise the
+// int8 weight rows of each stage to bf16/f16 in shared memory, and the last
+// four warps drain the double-buffered TMEM accumulator (lane quarter =
+// warp % 4) and store.
 // Every mbarrier wait is bounded (ptx.cuh); on expiry the CTA drains its
 // in-flight copies and MMAs, frees TMEM and returns with MOE_ERR_TIMEOUT in the
 // status word. Group offsets are validated before use (MOE_ERR_BAD_OFFSETS).
@@ -260,20 +261,34 @@ __device__ __forceinline__ void store_block32_staged(uint4* stage, const float (
 }
 
 // Exact int8 -> 16-bit float for 16 packed bytes. Each signed byte b becomes
-// the f32 2^23 + (b + 128) by byte placement, minus 2^23 + 128.
+// the f32 2^23 + (b + 128) by byte placement, minus 2^23 + 128 -- two values
+// per packed f32x2 subtraction (sm_100). The results are integers in
+// [-128, 127], exact in bf16 and f16: bf16 keeps the f32's high half (a byte
+// permute), f16 converts.
+__device__ __forceinline__ uint64_t sub_magic_f32x2(uint32_t a, uint32_t b) {
+  const uint64_t x = (static_cast<uint64_t>(b) << 32) | a;
+  constexpr uint64_t kMagic = 0x4B0000804B000080ull;  // two f32 2^23 + 128
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(kMagic));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t pack_exact2(uint64_t ab, int f16) {
+  const uint32_t a = static_cast<uint32_t>(ab), b = static_cast<uint32_t>(ab >> 32);
+  if (f16) return pack2(__uint_as_float(a), __uint_as_float(b), 1);
+  return __byte_perm(a, b, 0x7632);
+}
+
 __device__ __forceinline__ void dequant16(uint4 q, int f16, uint4& lo, uint4& hi) {
   const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
   uint32_t out[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float f[4];
+    uint32_t bits[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const uint32_t bits = __byte_perm(w[i], 0x4B000000u, 0x7540u | static_cast<uint32_t>(b));
-      f[b] = __uint_as_float(bits) - 8388736.0f;
-    }
-    out[2 * i] = pack2(f[0], f[1], f16);
-    out[2 * i + 1] = pack2(f[2], f[3], f16);
+    for (int b = 0; b < 4; ++b) bits[b] = __byte_perm(w[i], 0x4B000000u, 0x7540u | static_cast<uint32_t>(b));
+    out[2 * i] = pack_exact2(sub_magic_f32x2(bits[0], bits[1]), f16);
+    out[2 * i + 1] = pack_exact2(sub_magic_f32x2(bits[2], bits[3]), f16);
   }
   lo = make_uint4(out[0], out[1], out[2], out[3]);
   hi = make_uint4(out[4], out[5], out[6], out[7]);

@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) grouped_gemm_pair_kernel(cons
         decode_tile(c, p, t, tl, RT);
         const Segment& Sg = p.seg[tl.seg];
         const uint32_t idesc = idesc_f16(2 * BM, Sg.mma_n, p.in_f16 != 0);
-        if (!wait_parity_bounded(&c.tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
+        // the epilogue warps of both CTAs release the accumulator (release.cluster)
+        if (!wait_parity_bounded<true>(&c.tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         for (int kb = tl.kb0; kb < tl.kb1; ++kb) {

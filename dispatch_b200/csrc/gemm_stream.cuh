@@ -134,24 +134,6 @@ __device__ __forceinline__ void decode_stream_tile(const StreamCtrl& c, const St
   tl.rows = min(nt, c.off[s][lo + 1] - tl.row0);
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// All `count` threads of barrier `id` get the AND of their predicates.
-__device__ __forceinline__ bool named_bar_and(int id, int count, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
-      : "memory");
-  return out != 0;
-}
-
 __device__ __forceinline__ uint16_t to16(float v, int f16) {
   return static_cast<uint16_t>(pack2(v, 0.f, f16) & 0xFFFFu);
 }

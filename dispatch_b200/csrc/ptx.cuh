@@ -65,15 +65,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test with acquire semantics at cluster scope: for a barrier on
+// which threads of the other CTA of a pair arrive (release.cluster).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises *abort) when the wait exceeds kWaitLimitNs or another role of the CTA
 // already aborted; the caller then unwinds without issuing more work.
+// kCluster: acquire at cluster scope.
+template <bool kCluster = false>
 __device__ __forceinline__ bool wait_parity_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
                                                     int32_t* status) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto test = [&] { return kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+  if (test()) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (test()) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -83,6 +100,25 @@ __device__ __forceinline__ bool wait_parity_bounded(uint64_t* bar, uint32_t pari
       }
     }
   }
+}
+
+// ---------------------------------------------------------------- named barriers
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// All `count` threads of barrier `id` get the AND of their predicates.
+__device__ __forceinline__ bool named_bar_and(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
 }
 
 // ---------------------------------------------------------------- TMA
