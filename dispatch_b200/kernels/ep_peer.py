@@ -265,34 +265,48 @@ class PeerEPLayer:
         x = x.contiguous()
         out = torch.empty(t, h, dtype=x.dtype, device=dev)
         if self.chunks == 1 or t < self.chunk_min_tokens:
-            self._forward(x, out, self.buf, dev, mark=True)
+            self._forward(x, out, None, self.buf, dev, mark=True)
             return out
-        # every rank splits the same way and makes the same exchange calls on
-        # each chunk's buffers, in the same order
+        # Every rank splits the same way and makes the same exchange calls on
+        # each chunk's buffers, in the same order. All chunks are routed and
+        # grouped first (their router GEMM could not start beside a running
+        # FFN, whose CTAs fill every SM); chunk c then runs on its own stream
+        # once chunk c-1's rows are dispatched, so its count exchange and
+        # dispatch (NVLink stores from a few CTAs) overlap chunk c-1's FFN.
         bounds = [t * c // self.chunks for c in range(self.chunks + 1)]
+        preps = [self._route_group(x[bounds[c]:bounds[c + 1]]) for c in range(self.chunks)]
         main = torch.cuda.current_stream(dev)
-        for c in range(self.chunks):
-            lo, hi = bounds[c], bounds[c + 1]
-            if c == 0:
-                self._forward(x[lo:hi], out[lo:hi], self.buf, dev, mark=True)
-                continue
+        gate = self._forward(x[bounds[0]:bounds[1]], out[bounds[0]:bounds[1]], preps[0], self.buf, dev, mark=True)
+        for c in range(1, self.chunks):
             s = self._chunk_streams[c - 1]
-            s.wait_stream(main)
+            s.wait_event(gate)
             with torch.cuda.stream(s):
-                self._forward(x[lo:hi], out[lo:hi], self._chunk_bufs[c - 1], dev, mark=False)
+                gate = self._forward(x[bounds[c]:bounds[c + 1]], out[bounds[c]:bounds[c + 1]], preps[c],
+                                     self._chunk_bufs[c - 1], dev, mark=False)
             x.record_stream(s)
             out.record_stream(s)
+            for tsr in preps[c]:
+                tsr.record_stream(s)
         for s in self._chunk_streams:
             main.wait_stream(s)
         return out
 
-    def _forward(self, x: torch.Tensor, out: torch.Tensor, buf: PeerBuffers, dev: torch.device, *,
-                 mark: bool) -> None:
-        """One pass of the EP round trip for x (rows of this rank) through
-        `buf`, on the current stream; the combined rows go to `out`."""
+    def _route_group(self, x: torch.Tensor) -> tuple:
+        """Router and grouping of this rank's rows x on the current stream:
+        (ids, weights, counts, offsets, slot positions, f32 weights)."""
         from dispatch_b200.kernels.grouping import _group  # noqa: PLC0415
         from dispatch_b200.kernels.layer import route  # noqa: PLC0415
 
+        idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
+        counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
+        return idx, w, counts, offsets, pos, wf
+
+    def _forward(self, x: torch.Tensor, out: torch.Tensor, prep: tuple, buf: PeerBuffers, dev: torch.device, *,
+                 mark: bool) -> torch.cuda.Event:
+        """One pass of the EP round trip for x (rows of this rank, routed and
+        grouped in `prep`, or here if None) through `buf`, on the current stream; the combined
+        rows go to `out`. Returns an event recorded once the rows are
+        dispatched (after the barrier that follows the dispatch)."""
         t, h = x.shape
         if t > buf.max_tokens:
             raise ValueError(f"{t} tokens exceed the {buf.max_tokens} tokens per rank the peer buffers hold")
@@ -302,8 +316,7 @@ class PeerEPLayer:
         stream = L.stream_ptr(dev)
         k = self.top_k
         mark_fn("start")
-        idx, w = route(x, self.router_weight, self.cfg, e_score_bias=self.bias)
-        counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
+        idx, w, counts, offsets, pos, wf = self._route_group(x) if prep is None else prep
         mark_fn("route_group")
         sh = self.shared
         i_sh = 0 if sh is None else sh.gate.shape[0]
@@ -334,6 +347,8 @@ class PeerEPLayer:
         mark_fn("dispatch")
         buf.exchange(None, 1, epoch)
         mark_fn("barrier_after_dispatch")
+        dispatched = torch.cuda.Event()
+        dispatched.record()
         fused_shared = sh is not None and not overlap
         wq = self.weights
         g, u, d = (wq.gate.data, wq.up.data, wq.down.data) if self.quant else (wq.gate, wq.up, wq.down)
@@ -360,3 +375,4 @@ class PeerEPLayer:
                              out.data_ptr(), L.dt(out), st, stream)
         L.check(rc, "moe_combine")
         mark_fn("combine")
+        return dispatched
