@@ -10,8 +10,9 @@
  * int32 status word in device memory (first error wins; 0 = OK); the caller
  * reads it after synchronising. Calls are stream-ordered and thread-compatible:
  * one stream per call, no global mutable state apart from a per-device cache
- * of the SM count and the driver's tensor-map encoder, and the process-wide
- * FFN kernel choice of moe_set_ffn_kernel.
+ * of the SM count and the driver's tensor-map encoder, a per-device side
+ * stream of moe_layer_forward (one-token calls), and the process-wide FFN
+ * kernel choice of moe_set_ffn_kernel.
  *
  * Layouts (row-major, contiguous unless a leading dimension is passed):
  *   x            (T, H)        activations, bf16 / f16 / f32
@@ -253,6 +254,11 @@ int moe_quantize_int8(const void* w, int w_dtype, int64_t rows, int64_t K, int8_
  * skipped. Outputs: out (T, H) in out_dtype; topk_idx/topk_w (T,k) (written by
  * the router, or copies of the inputs are not made: pass the same buffers),
  * counts (E), offsets (E+1) (all may be NULL except out).
+ * With a shared expert and T = 1 the shared expert runs on a second stream
+ * of the library's (one per device, made by the first such call: make it
+ * before capturing the call in a CUDA graph), forked from `stream` with an
+ * event and joined before the combine; host threads that call this on one
+ * device at once take turns for that part of the enqueue.
  */
 typedef struct MoeLayerDesc {
   int64_t T, H, E, I, I_shared;
