@@ -459,7 +459,11 @@ def router_id_agreement(x, router, cfg, bias) -> dict:
             "vs": "float64 torch selection from float64 logits"}
 
 
-def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
+def time_loop(fn, steps: int, warmup: int, world: int, stream, per_step: list | None = None) -> float:
+    """Mean device time of one step (ms) over `steps` timed calls after
+    `warmup` untimed ones, CUDA events on `stream`, barriers on both sides.
+    If `per_step` is a list, each step's own duration (ms) is appended to it
+    (an event between consecutive steps; the total is unchanged)."""
     import torch
 
     for _ in range(warmup):
@@ -467,15 +471,29 @@ def time_loop(fn, steps: int, warmup: int, world: int, stream) -> float:
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1 if per_step is not None else 2)]
+    marks[0].record(stream)
+    for i in range(steps):
         fn()
-    end.record(stream)
+        if per_step is not None:
+            marks[i + 1].record(stream)
+    marks[-1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    return start.elapsed_time(end) / steps
+    if per_step is not None:
+        per_step.extend(marks[i].elapsed_time(marks[i + 1]) for i in range(steps))
+    return marks[0].elapsed_time(marks[-1]) / steps
+
+
+def step_stats(per_step: list, world: int) -> dict:
+    """Median and 99th percentile of the per-step times (ms), max over ranks."""
+    import statistics
+
+    v = sorted(per_step)
+    med = statistics.median(v)
+    p99 = v[min(len(v) - 1, int(round(0.99 * (len(v) - 1))))]
+    return {"median_ms": round(max_over_ranks(med, world), 4), "p99_ms": round(max_over_ranks(p99, world), 4),
+            "steps": len(v)}
 
 
 def host_copy_ceiling(x_host, out_host, dev, world: int, n: int = 20) -> float:
@@ -605,8 +623,10 @@ def run_b200(args, wl: Workload) -> None:
     torch.cuda.synchronize()
 
     with ClockSampler(local) as clocks:
-        ms = time_loop(lambda: layer(x), args.steps, args.warmup, world, stream)
+        per_step: list = []
+        ms = time_loop(lambda: layer(x), args.steps, args.warmup, world, stream, per_step)
     ms = max_over_ranks(ms, world)
+    step_dist = step_stats(per_step, world)
     L.check_device_status(dev)
     value = t * world / (ms * 1e-3)
 
@@ -684,7 +704,8 @@ def run_b200(args, wl: Workload) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "step_ms": step_dist,
+            "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if not wl.int8 else "bf16 x int8",
             "data": "synthetic",
             "config": {"workload": f"{wl.desc}, T={t} tokens/GPU, {args.routing} routing",

@@ -100,7 +100,7 @@ def test_rows_do_not_depend_on_tile_width() -> None:
     big_sizes = [600, 3, 700, 0, 512, 129, 900, 2]
     xb = randn((sum(big_sizes), k), g, 1.0)
     big = grouped_matmul(xb, w, build_tile_schedule(torch.tensor(big_sizes, device=DEV), 16))
-    # two rows of expert 1 and one of expert 7, alone: a handful of tiles -> narrow MMA width
+    # two rows of expert 1 and one of expert 7, alone: a handful of tiles
     rows = [600, 601, sum(big_sizes) - 1]
     small_sizes = [0, 2, 0, 0, 0, 0, 0, 1]
     small = grouped_matmul(xb[rows].contiguous(), w, build_tile_schedule(torch.tensor(small_sizes, device=DEV), 16))

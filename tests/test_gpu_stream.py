@@ -26,7 +26,7 @@ from gpu_helpers import LayerWeights, assert_parity, np32, randn  # noqa: E402
 from dispatch_b200 import _lib as L  # noqa: E402
 from dispatch_b200.kernels.grouped_gemm import grouped_matmul  # noqa: E402
 from dispatch_b200.kernels.grouped_gemm_int8 import grouped_matmul_int8  # noqa: E402
-from dispatch_b200.kernels.layer import RouterConfig, moe_layer_forward  # noqa: E402
+from dispatch_b200.kernels.layer import CapturedLayer, RouterConfig, moe_layer_forward  # noqa: E402
 from dispatch_b200.kernels.moe_forward import SharedExpertWeights, StackedExpertWeights  # noqa: E402
 from dispatch_b200.kernels.quantization import quantize_per_channel_int8, quantize_stacked_weights  # noqa: E402
 from dispatch_b200.kernels.tile_schedule import build_tile_schedule  # noqa: E402
@@ -168,3 +168,23 @@ def test_pair_layer_equals_tiled(c2: LayerWeights, t: int) -> None:
         a, b = _pair_vs_tiled(lambda: moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6), shared=sh,
                                                         e_score_bias=bias).out)
         assert torch.equal(a, b), f"T={t}: max |diff| {(a.float() - b.float()).abs().max().item()}"
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_one_token_call_forks_the_shared_expert_with_the_same_bits(c2: LayerWeights, quant: bool) -> None:
+    """A one-token layer call runs the shared expert on a second stream beside
+    the routed path; a larger batch runs it inside the routed launches. Each
+    token's row must come out the same either way, eager and captured in a
+    CUDA graph."""
+    ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
+    if quant:
+        ws = quantize_stacked_weights(ws, scale_dtype=torch.bfloat16)
+    cfg = RouterConfig(top_k=6)
+    x = randn((5, 2048), torch.Generator(device="cuda").manual_seed(77), 1.0)
+    batch = moe_layer_forward(x, c2.router, ws, cfg, shared=sh).out
+    for i in range(5):
+        one = moe_layer_forward(x[i:i + 1].contiguous(), c2.router, ws, cfg, shared=sh).out
+        assert torch.equal(one[0], batch[i]), f"token {i}"
+    cap = CapturedLayer(x[2:3].contiguous(), c2.router, ws, cfg, shared=sh)
+    for _ in range(2):
+        assert torch.equal(cap.replay().out[0], batch[2])
