@@ -577,8 +577,7 @@ def run_b200(args, wl: Workload) -> None:
         if args.ep_transport == "peer":
             from dispatch_b200.kernels.ep_peer import PeerEPLayer
 
-            ep = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t,
-                             chunks=args.ep_chunks)
+            ep = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t)
         else:
             from dispatch_b200.kernels.expert_parallel import EPLayer
 
@@ -588,8 +587,7 @@ def run_b200(args, wl: Workload) -> None:
             return ep(xx)
 
         launches_per_step = ep.launches_for(t) if hasattr(ep, "launches_for") else ep.launches_per_step
-        parallelism = f"ep{world} ({args.ep_transport}" + (f", {args.ep_chunks} chunks)" if args.ep_chunks > 1 and
-                                                           args.ep_transport == "peer" else ")")
+        parallelism = f"ep{world} ({args.ep_transport})"
     else:
         def layer(xx):
             return moe_layer_forward(xx, router, ws, cfg, shared=sh, e_score_bias=bias).out
@@ -837,9 +835,6 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: NVLink peer stores fused into dispatch/FFN (peer) or NCCL all-to-all (nccl)")
-    ap.add_argument("--ep-chunks", type=int, default=1,
-                    help="N>1, peer transport: split each call's tokens into this many chunks on their own streams "
-                         "so one chunk's dispatch overlaps the previous chunk's FFN")
     ap.add_argument("--profile-calls", type=int, default=0,
                     help="run the layer this many times and exit (a driver for ncu launch lists and captures)")
     ap.add_argument("--profile-ep-sim", type=int, default=0, metavar="W",

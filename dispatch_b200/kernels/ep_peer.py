@@ -155,7 +155,7 @@ class PeerEPLayer:
                  e_score_bias=None, n_experts: int | None = None, weights_are_local: bool = False,
                  max_tokens: int = 4096, act_dtype: torch.dtype = torch.bfloat16,
                  buffers: PeerBuffers | None = None, overlap_shared: bool = False,
-                 overlap_min_tokens: int = 1024, chunks: int = 1, chunk_min_tokens: int = 1024):
+                 overlap_min_tokens: int = 1024):
         from dispatch_b200.kernels.expert_parallel import _slice_experts  # noqa: PLC0415
         from dispatch_b200.kernels.quantization import QuantizedStackedExpertWeights  # noqa: PLC0415
 
@@ -185,32 +185,13 @@ class PeerEPLayer:
         # of at least overlap_min_tokens tokens split it off. Off by default:
         # at 8 GPUs the step was slower with it (0.92 ms), the shared GEMM's
         # persistent CTAs leaving one dispatch CTA per SM for 7x more rows.
-        self.overlap_shared = overlap_shared and shared is not None and chunks == 1
+        self.overlap_shared = overlap_shared and shared is not None
         self.overlap_min_tokens = overlap_min_tokens
         self._side: torch.cuda.Stream | None = None
-        # Chunked calls: a call of at least chunk_min_tokens tokens is split
-        # into `chunks` row ranges, each run through its own peer buffers on
-        # its own stream, so chunk c+1's routing, count exchange and NVLink
-        # dispatch run while chunk c's FFN has the tensor cores (the small
-        # dispatch and exchange CTAs fit beside the FFN's persistent CTA on
-        # each SM). Rows are independent and the router is batch-invariant, so
-        # the output is the same bits as one unchunked call. Chunk 0 uses
-        # `buffers` (sized for max_tokens); the others get buffers sized for
-        # ceil(max_tokens / chunks).
-        if chunks < 1:
-            raise ValueError(f"chunks={chunks} must be >= 1")
-        self.chunks, self.chunk_min_tokens = chunks, chunk_min_tokens
-        self._chunk_bufs = [
-            PeerBuffers(rank=rank, world=world, group=group, device=g.device,
-                        max_tokens=(max_tokens + chunks - 1) // chunks, top_k=self.top_k, hidden=self.hidden,
-                        n_experts=e, act_dtype=self.act_dtype)
-            for _ in range(chunks - 1)]
-        self._chunk_streams = [torch.cuda.Stream(g.device) for _ in range(chunks - 1)]
         # launches of this library per call: route x2, group x2, exchange x3, dispatch, FFN x2 (+2 shared), combine
         self.launches_per_step = 13 if self.overlap_shared else 11
         # Set to a list to have each call append (phase name, CUDA event)
-        # marks, recorded on the current stream after each phase (of the first
-        # chunk, in a chunked call).
+        # marks, recorded on the current stream after each phase.
         self.phase_events: list | None = None
 
     PHASES = ("route_group", "count_exchange", "dispatch", "barrier_after_dispatch", "ffn_and_return",
@@ -224,15 +205,10 @@ class PeerEPLayer:
 
     def launches_for(self, t: int) -> int:
         """Launches of this library in one call on t tokens."""
-        if self.chunks > 1 and t >= self.chunk_min_tokens:
-            return 11 * self.chunks
         return 13 if (self.overlap_shared and t >= self.overlap_min_tokens) else 11
 
     def close(self) -> None:
         """Collective: frees the peer buffers (every rank calls it)."""
-        for b in self._chunk_bufs:
-            b.close()
-        self._chunk_bufs = []
         if self._own_buffers:
             self.buf.close()
 
@@ -264,31 +240,7 @@ class PeerEPLayer:
             raise ValueError(f"x must be ({t}, {self.hidden}) {self.buf.act_dtype}, got {tuple(x.shape)} {x.dtype}")
         x = x.contiguous()
         out = torch.empty(t, h, dtype=x.dtype, device=dev)
-        if self.chunks == 1 or t < self.chunk_min_tokens:
-            self._forward(x, out, None, self.buf, dev, mark=True)
-            return out
-        # Every rank splits the same way and makes the same exchange calls on
-        # each chunk's buffers, in the same order. All chunks are routed and
-        # grouped first (their router GEMM could not start beside a running
-        # FFN, whose CTAs fill every SM); chunk c then runs on its own stream
-        # once chunk c-1's rows are dispatched, so its count exchange and
-        # dispatch (NVLink stores from a few CTAs) overlap chunk c-1's FFN.
-        bounds = [t * c // self.chunks for c in range(self.chunks + 1)]
-        preps = [self._route_group(x[bounds[c]:bounds[c + 1]]) for c in range(self.chunks)]
-        main = torch.cuda.current_stream(dev)
-        gate = self._forward(x[bounds[0]:bounds[1]], out[bounds[0]:bounds[1]], preps[0], self.buf, dev, mark=True)
-        for c in range(1, self.chunks):
-            s = self._chunk_streams[c - 1]
-            s.wait_event(gate)
-            with torch.cuda.stream(s):
-                gate = self._forward(x[bounds[c]:bounds[c + 1]], out[bounds[c]:bounds[c + 1]], preps[c],
-                                     self._chunk_bufs[c - 1], dev, mark=False)
-            x.record_stream(s)
-            out.record_stream(s)
-            for tsr in preps[c]:
-                tsr.record_stream(s)
-        for s in self._chunk_streams:
-            main.wait_stream(s)
+        self._forward(x, out, dev)
         return out
 
     def _route_group(self, x: torch.Tensor) -> tuple:
@@ -301,22 +253,18 @@ class PeerEPLayer:
         counts, offsets, pos, _, _, wf, _ = _group(idx, w, self.n_experts, want_sorted=False)
         return idx, w, counts, offsets, pos, wf
 
-    def _forward(self, x: torch.Tensor, out: torch.Tensor, prep: tuple, buf: PeerBuffers, dev: torch.device, *,
-                 mark: bool) -> torch.cuda.Event:
-        """One pass of the EP round trip for x (rows of this rank, routed and
-        grouped in `prep`, or here if None) through `buf`, on the current stream; the combined
-        rows go to `out`. Returns an event recorded once the rows are
-        dispatched (after the barrier that follows the dispatch)."""
+    def _forward(self, x: torch.Tensor, out: torch.Tensor, dev: torch.device) -> None:
+        """One pass of the EP round trip for x (rows of this rank) on the
+        current stream; the combined rows go to `out`."""
         t, h = x.shape
-        if t > buf.max_tokens:
-            raise ValueError(f"{t} tokens exceed the {buf.max_tokens} tokens per rank the peer buffers hold")
-        mark_fn = self._mark if mark else (lambda name: None)
+        buf = self.buf
+        mark_fn = self._mark
         lib = L.lib()
         st = L.status_word(dev).data_ptr()
         stream = L.stream_ptr(dev)
         k = self.top_k
         mark_fn("start")
-        idx, w, counts, offsets, pos, wf = self._route_group(x) if prep is None else prep
+        idx, w, counts, offsets, pos, wf = self._route_group(x)
         mark_fn("route_group")
         sh = self.shared
         i_sh = 0 if sh is None else sh.gate.shape[0]
@@ -347,8 +295,6 @@ class PeerEPLayer:
         mark_fn("dispatch")
         buf.exchange(None, 1, epoch)
         mark_fn("barrier_after_dispatch")
-        dispatched = torch.cuda.Event()
-        dispatched.record()
         fused_shared = sh is not None and not overlap
         wq = self.weights
         g, u, d = (wq.gate.data, wq.up.data, wq.down.data) if self.quant else (wq.gate, wq.up, wq.down)
@@ -375,4 +321,3 @@ class PeerEPLayer:
                              out.data_ptr(), L.dt(out), st, stream)
         L.check(rc, "moe_combine")
         mark_fn("combine")
-        return dispatched

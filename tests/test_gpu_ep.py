@@ -48,7 +48,7 @@ def _bias(dev, skew: bool):
 
 
 def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str, transport: str = "nccl",
-            quant: bool = False, chunks: int = 1) -> None:
+            quant: bool = False) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -69,8 +69,7 @@ def _worker(rank: int, world: int, port: int, t: int, skew: bool, out_dir: str, 
             ws = quantize_stacked_weights(ws)
         cfg, bias = RouterConfig(top_k=K), _bias(dev, skew)
         if transport == "peer":
-            layer = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t + 7,
-                                chunks=chunks, chunk_min_tokens=2)
+            layer = PeerEPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias, max_tokens=t + 7)
         else:
             layer = EPLayer(router, ws, sh, cfg, rank=rank, world=world, e_score_bias=bias)
         out = layer(x)
@@ -166,16 +165,12 @@ def _worlds() -> list[int]:
 
 
 @pytest.mark.parametrize("world", _worlds())
-@pytest.mark.parametrize("t,skew,quant,chunks", [(256, False, False, 1), (1024, True, False, 1), (1, False, False, 1),
-                                                 (300, True, True, 1), (1024, False, False, 2),
-                                                 (301, True, True, 3)])
-def test_peer_ep_output_is_byte_exact_vs_one_gpu(world: int, t: int, skew: bool, quant: bool, chunks: int,
-                                                 tmp_path) -> None:
+@pytest.mark.parametrize("t,skew,quant", [(256, False, False), (1024, True, False), (1, False, False),
+                                          (300, True, True)])
+def test_peer_ep_output_is_byte_exact_vs_one_gpu(world: int, t: int, skew: bool, quant: bool, tmp_path) -> None:
     """Dispatch by NVLink stores, FFN whose epilogue stores the rows back to
-    their source ranks: the same bytes as the 1-GPU layer -- also when a call
-    is split into row chunks that run on their own streams and buffers."""
+    their source ranks: the same bytes as the 1-GPU layer."""
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(world, _free_port(), t, skew, str(tmp_path), "peer", quant, chunks), nprocs=world,
-             join=True)
+    mp.spawn(_worker, args=(world, _free_port(), t, skew, str(tmp_path), "peer", quant), nprocs=world, join=True)
     _check_byte_exact(tmp_path, world, t, skew, quant)
