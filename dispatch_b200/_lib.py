@@ -27,7 +27,7 @@ MOE_ERR_BAD_EXPERT = 6
 MOE_ERR_BAD_OFFSETS = 7
 
 DT_BF16, DT_F16, DT_F32, DT_I8, DT_I32, DT_I64 = range(6)
-FFN_KERNEL_AUTO, FFN_KERNEL_TILED, FFN_KERNEL_STREAM, FFN_KERNEL_PAIR = range(4)
+FFN_KERNEL_AUTO, FFN_KERNEL_TILED, FFN_KERNEL_STREAM, FFN_KERNEL_PAIR, FFN_KERNEL_WARP = range(5)
 ROUTER_SOFTMAX, ROUTER_SIGMOID_GROUP = 0, 1
 
 _TORCH_DT = {

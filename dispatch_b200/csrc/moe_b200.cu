@@ -19,6 +19,7 @@
 #include "gemm.cuh"
 #include "gemm2sm.cuh"
 #include "gemm_stream.cuh"
+#include "gemm_warp.cuh"
 #include "group.cuh"
 #include "route.cuh"
 
@@ -397,6 +398,59 @@ int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* sta
   return launch_pair(p, static_cast<int>(2 * pairs), stream);
 }
 
+// ---------------------------------------------------------------- warp-MMA kernel
+int launch_warp(const moe::gemm::Params& p, int grid, cudaStream_t stream) {
+  constexpr size_t smem = moe::gemm::warp_smem_bytes();
+  static_assert(2 * (smem + 1024) <= 233472, "two warp-MMA CTAs per SM");
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(warp gemm)");
+  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_warp_kernel, dim3(grid), dim3(moe::gemm::kWThreads), smem, stream, p),
+           "grouped_gemm_warp_kernel launch");
+  return MOE_OK;
+}
+
+// The warp-MMA kernel over up to two FFN segments (16-bit weights, one K
+// range, no gathered rows, 16-bit outputs): tiles of 128 weight rows x up to
+// 32 token rows, two CTAs per SM.
+int run_gemm_warp(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
+  int sms = 0;
+  int rc = device_info(&sms);
+  if (rc) return rc;
+  moe::gemm::Params p;
+  std::memset(&p, 0, sizeof(p));
+  int64_t tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    SegSpec spec = specs_in[i];
+    CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
+              "the warp-MMA kernel takes 16-bit weights, one K range, no gathered rows, 16-bit outputs");
+    spec.mma_n = moe::gemm::kWRows;
+    spec.a_box_rows = moe::gemm::kWTok;
+    spec.b_box_rows = 0;  // 64 gate + 64 up rows, or 128 rows
+    rc = check_seg(spec, act_dtype);
+    if (rc) return rc;
+    rc = fill_segment(&p.seg[i], spec, act_dtype);
+    if (rc) return rc;
+    const int oc = spec.swiglu ? moe::gemm::kWRows / 2 : moe::gemm::kWRows;
+    const int64_t rt = moe::gemm::kWTok;
+    const int64_t mt = spec.offsets ? spec.a_rows / rt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
+                                    : (spec.a_rows + rt - 1) / rt;
+    tiles += mt * ((spec.N + oc - 1) / oc);
+    p.remote_out |= spec.out_rows ? 1 : 0;
+  }
+  p.num_segs = nseg;
+  p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
+  p.status = status;
+  const int64_t slots = 2 * static_cast<int64_t>(sms);
+  const int64_t grid = tiles < slots ? tiles : slots;
+  if (grid <= 0) return MOE_OK;
+  return launch_warp(p, static_cast<int>(grid), stream);
+}
+
 // ---------------------------------------------------------------- streaming kernel
 std::atomic<int> g_ffn_kernel{MOE_FFN_KERNEL_AUTO};
 
@@ -522,7 +576,7 @@ int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
 
 int moe_set_ffn_kernel(int choice) {
   if (choice != MOE_FFN_KERNEL_AUTO && choice != MOE_FFN_KERNEL_TILED && choice != MOE_FFN_KERNEL_STREAM &&
-      choice != MOE_FFN_KERNEL_PAIR)
+      choice != MOE_FFN_KERNEL_PAIR && choice != MOE_FFN_KERNEL_WARP)
     return -1;
   return g_ffn_kernel.exchange(choice);
 }
@@ -908,17 +962,25 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     ++n;
   }
   if (n == 0) return MOE_OK;
-  // Kernel choice per projection (every choice gives the same bits). AUTO:
-  // the streaming kernel for the gate/up projection of decode-sized batches
-  // (routed groups averaging at most kStreamMaxAvgRows rows, a shared expert
-  // of at most kStreamMaxSharedRows), the tiled kernel otherwise -- and for
-  // the down projection always, which the tiled kernel ran faster at every
-  // batch size measured (C2 T=1: 21 vs 33 us; T=16: 58 vs 89 us).
+  // Kernel choice per projection (every choice gives the same bits). AUTO,
+  // for decode-sized batches (routed groups averaging at most
+  // kStreamMaxAvgRows rows, a shared expert of at most kStreamMaxSharedRows):
+  // the warp-MMA kernel for both projections with 16-bit weights (C2 layer as
+  // a CUDA graph on B200, against the streaming gate/up + tiled down: T=1 81
+  // -> 71 us, T=4 137 -> 117 us, T=16 209 -> 190 us; slower from T=64 on),
+  // the streaming kernel for the gate/up projection with int8 weights; the
+  // tiled kernel otherwise -- and for an int8 down projection always, which
+  // the tiled kernel ran faster at every batch size measured (C2 T=1: 21 vs
+  // 33 us; T=16: 58 vs 89 us).
   const int choice = g_ffn_kernel.load();
   const bool streamable = !gather_rows;
   CHECK_ARG(choice != MOE_FFN_KERNEL_STREAM || streamable, "the streaming kernel does not take gathered rows");
   const bool small = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
-  const bool stream1 = choice == MOE_FFN_KERNEL_STREAM || (choice == MOE_FFN_KERNEL_AUTO && streamable && small);
+  const bool warpable = streamable && w_dtype != MOE_DT_I8;
+  CHECK_ARG(choice != MOE_FFN_KERNEL_WARP || warpable, "the warp-MMA kernel takes 16-bit weights and no gathered rows");
+  const bool warp_mma = choice == MOE_FFN_KERNEL_WARP || (choice == MOE_FFN_KERNEL_AUTO && warpable && small);
+  const bool stream1 = !warp_mma && (choice == MOE_FFN_KERNEL_STREAM ||
+                                     (choice == MOE_FFN_KERNEL_AUTO && streamable && small));
   const bool stream2 = choice == MOE_FFN_KERNEL_STREAM;
   // row tile per segment for the streaming kernel: about the rows a group
   // holds (routed: the average per group; shared: all of its rows), in [32, 256]
@@ -951,6 +1013,7 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
   const bool pair = choice == MOE_FFN_KERNEL_PAIR ||
                     (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && rows256 * 20 <= rows128 * 21);
   auto launch = [&](const SegSpec* g, bool stream_it) {
+    if (warp_mma) return run_gemm_warp(g, n, act_dtype, status, s);
     if (stream_it) return run_gemm_stream(g, nts, n, act_dtype, status, s);
     if (pair) return run_gemm_pair(g, n, act_dtype, status, s);
     return run_gemm(g, n, act_dtype, status, s);

@@ -188,3 +188,47 @@ def test_one_token_call_forks_the_shared_expert_with_the_same_bits(c2: LayerWeig
     cap = CapturedLayer(x[2:3].contiguous(), c2.router, ws, cfg, shared=sh)
     for _ in range(2):
         assert torch.equal(cap.replay().out[0], batch[2])
+
+
+def _warp_vs_tiled(fn):
+    with ffn_kernel(L.FFN_KERNEL_TILED):
+        a = fn()
+    with ffn_kernel(L.FFN_KERNEL_WARP):
+        b = fn()
+    torch.cuda.synchronize()
+    return a, b
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("sizes", "n", "k"), GEMM_CASES + [([40, 0, 1, 33, 7], 384, 2048)])
+def test_warp_grouped_matmul_equals_tiled(dtype, sizes, n, k) -> None:
+    """The warp-MMA kernel (eight warps per CTA, each a chain of mma.sync
+    m16n8k16 MMAs over K in order) gives the tiled tcgen05 kernel's bits:
+    groups longer than its 32-row token tile, empty groups, N and K not
+    multiples of the tile."""
+    g = torch.Generator(device="cuda").manual_seed(35)
+    sched = build_tile_schedule(torch.tensor(sizes, device=DEV), block_m=16)
+    x = randn((sum(sizes), k), g, 1.0, dtype)
+    w = randn((len(sizes), n, k), g, k ** -0.5, dtype)
+    a, b = _warp_vs_tiled(lambda: grouped_matmul(x, w, sched))
+    assert torch.equal(a, b), f"max |diff| {(a.float() - b.float()).abs().max().item()}"
+
+
+def test_warp_kernel_rejects_int8_weights(c2: LayerWeights) -> None:
+    ws = quantize_stacked_weights(StackedExpertWeights(c2.gate, c2.up, c2.down), scale_dtype=torch.bfloat16)
+    x = randn((4, 2048), torch.Generator(device="cuda").manual_seed(8), 1.0)
+    with ffn_kernel(L.FFN_KERNEL_WARP), pytest.raises(ValueError, match="16-bit weights"):
+        moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6))
+
+
+@pytest.mark.parametrize("t", [1, 7, 16, 64, 300])
+def test_warp_layer_equals_tiled(c2: LayerWeights, t: int) -> None:
+    """The whole C2 layer with both FFN projections on the warp-MMA kernel
+    (SwiGLU pairs exchanging accumulators through shared memory, the shared
+    expert as a dense segment): the tiled kernel's bits, uniform and Zipf."""
+    ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
+    x = randn((t, 2048), torch.Generator(device="cuda").manual_seed(970 + t), 1.0)
+    for bias in (None, -1.2 * torch.log(torch.arange(64, dtype=torch.float32, device=DEV) + 1.0)):
+        a, b = _warp_vs_tiled(lambda: moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6), shared=sh,
+                                                        e_score_bias=bias).out)
+        assert torch.equal(a, b), f"T={t}: max |diff| {(a.float() - b.float()).abs().max().item()}"
