@@ -17,45 +17,62 @@
 // the layer outputs of all kernels are compared in the tests), so the kernel
 // choice changes speed only.
 //
-// Unit of work (a "tile"): (segment, group, channel block, token block): 128
-// weight rows -- SwiGLU: 64 gate rows + the matching 64 up rows, plain: 128
-// output channels -- against up to 32 token rows of one group, over all of K.
-// Warp 0 lane 0 issues the TMA loads of each 64-wide k-block (the 128 weight
-// rows, 16 KiB, and the 32 token rows, 4 KiB, both 128-byte swizzled) into a
-// four-stage ring; MMA warp w (1..8) owns weight rows 16(w-1) .. 16(w-1)+15,
-// reads its operands with ldmatrix and keeps up to four 16x8 accumulators
-// (32 token rows). SwiGLU: the up warp of each pair hands its accumulators to
-// the matching gate warp through shared memory. Every wait is bounded; the two
-// warps of a pair agree on every wait's outcome before they meet, so a timeout
-// in one cannot leave the other waiting.
+// Unit of work (a "tile"): (segment, group, channel block, token block): 16 x
+// kWarps weight rows (128 or 64) -- SwiGLU: half gate rows + the matching up
+// rows, plain: output channels -- against a token tile of nt rows (8, 16 or
+// 32, per launch) of one group, over all of K. Warp 0 lane 0 issues the TMA
+// loads of each 64-wide k-block (the weight rows and the token rows, both
+// 128-byte swizzled) into a ring of four (128-row tiles) or eight (64-row
+// tiles) stages; MMA warp w (1..kWarps) owns weight rows 16(w-1) ..
+// 16(w-1)+15, reads its operands with ldmatrix and keeps up to four 16x8
+// accumulators (32 token rows). SwiGLU: the up warp of each pair hands its
+// accumulators to the matching gate warp through shared memory. Every wait is
+// bounded; the two warps of a pair agree on every wait's outcome before they
+// meet, so a timeout in one cannot leave the other waiting.
 #pragma once
 #include "gemm.cuh"
 
 namespace moe {
 namespace gemm {
 
-constexpr int kWarpMmaWarps = 8;
-constexpr int kWRows = 16 * kWarpMmaWarps;  // weight rows per tile
-constexpr int kWTok = 32;                   // token rows per tile (four n8 MMA tiles)
-constexpr int kWStages = 4;
-constexpr uint32_t kWWBytes = kWRows * BK * 2;  // 16 KiB of weights per k-block
-constexpr uint32_t kWXBytes = kWTok * BK * 2;   // 4 KiB of token rows per k-block
-constexpr uint32_t kWStageBytes = kWWBytes + kWXBytes;
-constexpr int kWThreads = 32 * (1 + kWarpMmaWarps);
+constexpr int kWTok = 32;  // most token rows per tile (four n8 MMA tiles)
+constexpr uint32_t kWXBytes = kWTok * BK * 2;  // token-row slot of a stage: 4 KiB
+
+// kWarps MMA warps own 16 weight rows each: 8 warps (128-row tiles, four
+// stages, two CTAs per SM) when a launch has many tiles, 4 warps (64-row
+// tiles, eight stages, two CTAs per SM) when it has few, so that a decode
+// step's few tiles still keep enough weight bytes in flight per SM.
+template <int kWarps>
+struct WarpConfig {
+  static constexpr int kRows = 16 * kWarps;
+  static constexpr int kStages = kWarps == 8 ? 4 : 8;
+  static constexpr uint32_t kWBytes = kRows * BK * 2;
+  static constexpr int kThreads = 32 * (1 + kWarps);
+  static constexpr int kPairs = kWarps / 2;  // SwiGLU: gate warp w with up warp w + kPairs
+};
 
 struct WarpCtrl {
-  uint64_t full[kWStages];
-  uint64_t empty[kWStages];
+  uint64_t full[8];
+  uint64_t empty[8];
   int abort;
   int seg_tiles[kMaxSegs];
   int off[kMaxSegs][kMaxGroups + 1];
   int mt[kMaxSegs][kMaxGroups + 1];
 };
 constexpr uint32_t kWCtrlBytes = (sizeof(WarpCtrl) + 15) & ~uint32_t(15);
-// the up warps' accumulators for the gate warps: 4 pairs x 32 lanes x 16 floats
+// the up warps' accumulators for the gate warps: up to 4 pairs x 32 lanes x 16 floats
 constexpr uint32_t kWXchgBytes = 4 * 32 * 16 * 4;
 
-constexpr size_t warp_smem_bytes() { return 1024 + kWStages * kWStageBytes + kWCtrlBytes + kWXchgBytes; }
+template <int kWarps>
+constexpr size_t warp_smem_bytes() {
+  return 1024 + WarpConfig<kWarps>::kStages * (WarpConfig<kWarps>::kWBytes + kWXBytes) + kWCtrlBytes + kWXchgBytes;
+}
+
+// One launch: the segments and the token-row tile (8, 16 or 32) of every tile.
+struct WarpParams {
+  Params p;
+  int nt;
+};
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -105,14 +122,21 @@ __device__ __forceinline__ void warp_store(const Params& p, const Segment& Sg, i
   obase[orow * Sg.ldo + ch] = static_cast<uint16_t>(pack2(v, 0.f, p.in_f16) & 0xFFFFu);
 }
 
-// Segments: mma_n = 128 (SwiGLU: 64 output channels per tile, plain: 128),
-// 16-bit weights, one K range, 16-bit outputs, no gathered rows.
-__global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __grid_constant__ Params p) {
-  constexpr int S = kWStages;
+// Segments: mma_n = 16 x kWarps (SwiGLU: half of it output channels per
+// tile), 16-bit weights, one K range, 16-bit outputs, no gathered rows.
+template <int kWarps>
+__global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
+    grouped_gemm_warp_kernel(const __grid_constant__ WarpParams wp) {
+  using Cfg = WarpConfig<kWarps>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kWWBytes = Cfg::kWBytes;
+  constexpr int kWThreads = Cfg::kThreads;
+  const Params& p = wp.p;
+  const int nt_tile = wp.nt;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sW = base;                   // S x 16 KiB (1024-aligned)
-  uint8_t* sX = sW + S * kWWBytes;      // S x 4 KiB (1024-aligned)
+  uint8_t* sW = base;                   // S weight slots (1024-aligned)
+  uint8_t* sX = sW + S * kWWBytes;      // S token-row slots of 4 KiB (1024-aligned)
   WarpCtrl& c = *reinterpret_cast<WarpCtrl*>(sX + S * kWXBytes);
   float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(&c) + kWCtrlBytes);
   volatile int* abort_flag = &c.abort;
@@ -125,7 +149,7 @@ __global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __gr
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&c.full[i], 1);
-      mbar_init(&c.empty[i], kWarpMmaWarps);
+      mbar_init(&c.empty[i], kWarps);
     }
     c.abort = 0;
     fence_mbar_init();
@@ -154,7 +178,7 @@ __global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __gr
       if (g < Sg.groups) {
         const int rows = c.off[s][g + 1] - c.off[s][g];
         bad |= rows < 0;
-        v = rows > 0 ? (rows + kWTok - 1) / kWTok : 0;
+        v = rows > 0 ? (rows + nt_tile - 1) / nt_tile : 0;
       }
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
@@ -183,12 +207,12 @@ __global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __gr
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         Tile tl;
-        decode_tile(c, p, t, tl, kWTok);
+        decode_tile(c, p, t, tl, nt_tile);
         const Segment& Sg = p.seg[tl.seg];
         const int n0 = tl.n_tile * out_cols_per_tile(Sg);
         for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
           if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&c.full[stage], kWStageBytes);
+          mbar_arrive_expect_tx(&c.full[stage], kWWBytes + static_cast<uint32_t>(nt_tile) * BK * 2);
           uint8_t* w_dst = sW + stage * kWWBytes;
           tma_load_2d(sX + stage * kWXBytes, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
           tma_load_3d(w_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
@@ -211,9 +235,9 @@ __global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __gr
     }
   } else {
     // ------------------------------------------------------------ MMA warps + epilogue
-    const int w = warp - 1;      // owns weight rows 16w .. 16w+15 of each stage
-    const int pair = w & 3;      // SwiGLU: gate warp w (< 4) with up warp w + 4
-    const bool up_warp = w >= 4;
+    const int w = warp - 1;                  // owns weight rows 16w .. 16w+15 of each stage
+    const int pair = w % Cfg::kPairs;        // SwiGLU: gate warp w (< kPairs) with up warp w + kPairs
+    const bool up_warp = w >= Cfg::kPairs;
     const int g = lane >> 2, tq = lane & 3;
     // ldmatrix row addresses: A (weights) x4 = rows 0-7 / 8-15 x k 0-7 / 8-15;
     // B (tokens) x4 = tokens 0-7 x k 0-7, k 8-15, tokens 8-15 x k 0-7, k 8-15
@@ -225,9 +249,9 @@ __global__ void __launch_bounds__(kWThreads) grouped_gemm_warp_kernel(const __gr
     bool ok = true;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       Tile tl;
-      decode_tile(c, p, t, tl, kWTok);
+      decode_tile(c, p, t, tl, nt_tile);
       const Segment& Sg = p.seg[tl.seg];
-      const int nt = (tl.rows + 7) >> 3;  // n8 token tiles in use (1..4)
+      const int nt = (tl.rows + 7) >> 3;  // n8 token tiles in use (1 .. nt_tile / 8)
       float acc[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j)

@@ -399,56 +399,78 @@ int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* sta
 }
 
 // ---------------------------------------------------------------- warp-MMA kernel
-int launch_warp(const moe::gemm::Params& p, int grid, cudaStream_t stream) {
-  constexpr size_t smem = moe::gemm::warp_smem_bytes();
+template <int kWarps>
+int launch_warp(const moe::gemm::WarpParams& wp, int grid, cudaStream_t stream) {
+  constexpr size_t smem = moe::gemm::warp_smem_bytes<kWarps>();
   static_assert(2 * (smem + 1024) <= 233472, "two warp-MMA CTAs per SM");
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem));
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_warp_kernel<kWarps>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(warp gemm)");
-  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_warp_kernel, dim3(grid), dim3(moe::gemm::kWThreads), smem, stream, p),
+  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_warp_kernel<kWarps>, dim3(grid),
+                      dim3(moe::gemm::WarpConfig<kWarps>::kThreads), smem, stream, wp),
            "grouped_gemm_warp_kernel launch");
   return MOE_OK;
 }
 
 // The warp-MMA kernel over up to two FFN segments (16-bit weights, one K
-// range, no gathered rows, 16-bit outputs): tiles of 128 weight rows x up to
-// 32 token rows, two CTAs per SM.
-int run_gemm_warp(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
+// range, no gathered rows, 16-bit outputs), two CTAs per SM. Tiles of 64
+// weight rows (four MMA warps, eight stages) when even twice as many tiles as
+// 128-row ones leave CTA slots free -- a decode step's few tiles then use
+// twice the SMs with the same weight bytes in flight per tile (C2 T=1 layer
+// graph 73.3 -> 71.2 us) -- else of 128 rows (eight warps, four stages: with
+// 64-row tiles beyond the slots, T=2 was 80 -> 99 us); the token-row tile is
+// the smallest of 8 / 16 / 32 that holds the average group.
+int run_gemm_warp(const SegSpec* specs_in, int nseg, const int64_t* avg_rows, int act_dtype, int32_t* status,
+                  cudaStream_t stream) {
   int sms = 0;
   int rc = device_info(&sms);
   if (rc) return rc;
-  moe::gemm::Params p;
-  std::memset(&p, 0, sizeof(p));
+  int64_t most = 1;
+  for (int i = 0; i < nseg; ++i) most = avg_rows[i] > most ? avg_rows[i] : most;
+  const int nt = most <= 8 ? 8 : most <= 16 ? 16 : moe::gemm::kWTok;
+  const int64_t slots = 2 * static_cast<int64_t>(sms);
+  // tiles with 128-row weight blocks
+  int64_t tiles128 = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const SegSpec& spec = specs_in[i];
+    const int oc = spec.swiglu ? 64 : 128;
+    const int64_t mt = spec.offsets ? spec.a_rows / nt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
+                                    : (spec.a_rows + nt - 1) / nt;
+    tiles128 += mt * ((spec.N + oc - 1) / oc);
+  }
+  const int warps = 2 * tiles128 <= slots ? 4 : 8;
+  moe::gemm::WarpParams wp;
+  std::memset(&wp, 0, sizeof(wp));
+  wp.nt = nt;
   int64_t tiles = 0;
   for (int i = 0; i < nseg; ++i) {
     SegSpec spec = specs_in[i];
     CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
               "the warp-MMA kernel takes 16-bit weights, one K range, no gathered rows, 16-bit outputs");
-    spec.mma_n = moe::gemm::kWRows;
-    spec.a_box_rows = moe::gemm::kWTok;
-    spec.b_box_rows = 0;  // 64 gate + 64 up rows, or 128 rows
+    spec.mma_n = 16 * warps;
+    spec.a_box_rows = nt;
+    spec.b_box_rows = 0;  // half gate, half up rows, or all rows
     rc = check_seg(spec, act_dtype);
     if (rc) return rc;
-    rc = fill_segment(&p.seg[i], spec, act_dtype);
+    rc = fill_segment(&wp.p.seg[i], spec, act_dtype);
     if (rc) return rc;
-    const int oc = spec.swiglu ? moe::gemm::kWRows / 2 : moe::gemm::kWRows;
-    const int64_t rt = moe::gemm::kWTok;
-    const int64_t mt = spec.offsets ? spec.a_rows / rt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
-                                    : (spec.a_rows + rt - 1) / rt;
+    const int oc = spec.swiglu ? 8 * warps : 16 * warps;
+    const int64_t mt = spec.offsets ? spec.a_rows / nt + (spec.G < spec.a_rows ? spec.G : spec.a_rows)
+                                    : (spec.a_rows + nt - 1) / nt;
     tiles += mt * ((spec.N + oc - 1) / oc);
-    p.remote_out |= spec.out_rows ? 1 : 0;
+    wp.p.remote_out |= spec.out_rows ? 1 : 0;
   }
-  p.num_segs = nseg;
-  p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
-  p.status = status;
-  const int64_t slots = 2 * static_cast<int64_t>(sms);
+  wp.p.num_segs = nseg;
+  wp.p.in_f16 = act_dtype == MOE_DT_F16 ? 1 : 0;
+  wp.p.status = status;
   const int64_t grid = tiles < slots ? tiles : slots;
   if (grid <= 0) return MOE_OK;
-  return launch_warp(p, static_cast<int>(grid), stream);
+  return warps == 8 ? launch_warp<8>(wp, static_cast<int>(grid), stream)
+                    : launch_warp<4>(wp, static_cast<int>(grid), stream);
 }
 
 // ---------------------------------------------------------------- streaming kernel
@@ -1012,8 +1034,14 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
   }
   const bool pair = choice == MOE_FFN_KERNEL_PAIR ||
                     (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && rows256 * 20 <= rows128 * 21);
+  int64_t avg_rows[2] = {1, 1};  // rows of the average group per segment (warp-MMA token tile)
+  {
+    int i = 0;
+    if (R > 0) avg_rows[i++] = (R + G - 1) / G;
+    if (has_shared) avg_rows[i++] = T_shared;
+  }
   auto launch = [&](const SegSpec* g, bool stream_it) {
-    if (warp_mma) return run_gemm_warp(g, n, act_dtype, status, s);
+    if (warp_mma) return run_gemm_warp(g, n, avg_rows, act_dtype, status, s);
     if (stream_it) return run_gemm_stream(g, nts, n, act_dtype, status, s);
     if (pair) return run_gemm_pair(g, n, act_dtype, status, s);
     return run_gemm(g, n, act_dtype, status, s);
