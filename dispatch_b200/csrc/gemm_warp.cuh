@@ -122,9 +122,20 @@ __device__ __forceinline__ void warp_store(const Params& p, const Segment& Sg, i
   obase[orow * Sg.ldo + ch] = static_cast<uint16_t>(pack2(v, 0.f, p.in_f16) & 0xFFFFu);
 }
 
+// Exact int8 -> bf16/f16 of two packed bytes (the low byte in the low half).
+__device__ __forceinline__ uint32_t cvt_i8x2(uint32_t v, int f16) {
+  const uint32_t w = (v ^ 0x8080u) & 0xFFFFu;
+  return pack_exact2(sub_magic_f32x2(__byte_perm(w, 0x4B000000u, 0x7540u), __byte_perm(w, 0x4B000000u, 0x7541u)),
+                     f16);
+}
+
 // Segments: mma_n = 16 x kWarps (SwiGLU: half of it output channels per
-// tile), 16-bit weights, one K range, 16-bit outputs, no gathered rows.
-template <int kWarps>
+// tile), 16-bit weights -- or, in the int8 build, int8 weights with
+// per-channel scales applied in the epilogue as in the tiled kernel -- one K
+// range, 16-bit outputs, no gathered rows. An int8 stage holds the weight rows
+// as 64-byte unswizzled rows; each MMA warp converts its own 16 rows straight
+// into the MMA's operand registers (exact), so no converted copy is written.
+template <int kWarps, bool kInt8>
 __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
     grouped_gemm_warp_kernel(const __grid_constant__ WarpParams wp) {
   using Cfg = WarpConfig<kWarps>;
@@ -212,11 +223,13 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
         const int n0 = tl.n_tile * out_cols_per_tile(Sg);
         for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
           if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&c.full[stage], kWWBytes + static_cast<uint32_t>(nt_tile) * BK * 2);
+          const bool q8 = kInt8 && Sg.b_int8;
+          const uint32_t w_bytes = q8 ? kWWBytes / 2 : kWWBytes;  // int8: 64-byte rows
+          mbar_arrive_expect_tx(&c.full[stage], w_bytes + static_cast<uint32_t>(nt_tile) * BK * 2);
           uint8_t* w_dst = sW + stage * kWWBytes;
           tma_load_2d(sX + stage * kWXBytes, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
           tma_load_3d(w_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
-          if (Sg.swiglu) tma_load_3d(w_dst + kWWBytes / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
+          if (Sg.swiglu) tma_load_3d(w_dst + w_bytes / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -251,6 +264,7 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
       Tile tl;
       decode_tile(c, p, t, tl, nt_tile);
       const Segment& Sg = p.seg[tl.seg];
+      const bool q8 = kInt8 && Sg.b_int8;
       const int nt = (tl.rows + 7) >> 3;  // n8 token tiles in use (1 .. nt_tile / 8)
       float acc[4][4];
 #pragma unroll
@@ -264,10 +278,20 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         const uint32_t wbase = smem_u32(sW + stage * kWWBytes);
         const uint32_t xbase = smem_u32(sX + stage * kWXBytes);
+        // int8: this thread's bytes (rows g and g + 8, k = 2tq.. and 8 + 2tq..)
+        const uint8_t* q0 = sW + stage * kWWBytes + (16 * w + g) * BK + 2 * tq;
 #pragma unroll
         for (int s = 0; s < BK / 16; ++s) {
           uint32_t a[4];
-          ldsm_x4(sw128_addr(wbase, a_row, 2 * s + a_khalf), a[0], a[1], a[2], a[3]);
+          if (q8) {
+            const uint8_t* qs = q0 + 16 * s;
+            a[0] = cvt_i8x2(*reinterpret_cast<const uint16_t*>(qs), p.in_f16);
+            a[1] = cvt_i8x2(*reinterpret_cast<const uint16_t*>(qs + 8 * BK), p.in_f16);
+            a[2] = cvt_i8x2(*reinterpret_cast<const uint16_t*>(qs + 8), p.in_f16);
+            a[3] = cvt_i8x2(*reinterpret_cast<const uint16_t*>(qs + 8 * BK + 8), p.in_f16);
+          } else {
+            ldsm_x4(sw128_addr(wbase, a_row, 2 * s + a_khalf), a[0], a[1], a[2], a[3]);
+          }
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
             if (2 * jj < nt) {
@@ -284,6 +308,7 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
       }
       const int oc = out_cols_per_tile(Sg);
       const int n0 = tl.n_tile * oc;
+      const int64_t sc_base = static_cast<int64_t>(tl.widx) * Sg.n;
       if (Sg.swiglu) {
         // both warps of a pair leave together or not at all
         ok = named_bar_and(1 + pair, 64, ok);
@@ -304,8 +329,12 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
               const int tok = 8 * j + 2 * tq + (e & 1);
               const int ch = n0 + 16 * w + g + ((e >> 1) << 3);
               if (j < nt && tok < tl.rows && ch < Sg.n) {
-                const float gv = acc[j][e];
-                const float uv = xb[4 * j + e];
+                float gv = acc[j][e];
+                float uv = xb[4 * j + e];
+                if (q8) {
+                  gv *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + ch);
+                  uv *= ld_scale(Sg.scale1, Sg.scale_bf16, sc_base + ch);
+                }
                 warp_store(p, Sg, tl.row0 + tok, ch, gv / (1.0f + __expf(-gv)) * uv);
               }
             }
@@ -320,7 +349,11 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
           for (int e = 0; e < 4; ++e) {
             const int tok = 8 * j + 2 * tq + (e & 1);
             const int ch = n0 + 16 * w + g + ((e >> 1) << 3);
-            if (j < nt && tok < tl.rows && ch < Sg.n) warp_store(p, Sg, tl.row0 + tok, ch, acc[j][e]);
+            if (j < nt && tok < tl.rows && ch < Sg.n) {
+              float o = acc[j][e];
+              if (q8) o *= ld_scale(Sg.scale0, Sg.scale_bf16, sc_base + ch);
+              warp_store(p, Sg, tl.row0 + tok, ch, o);
+            }
           }
         }
       }

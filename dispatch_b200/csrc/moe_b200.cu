@@ -399,25 +399,25 @@ int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* sta
 }
 
 // ---------------------------------------------------------------- warp-MMA kernel
-template <int kWarps>
+template <int kWarps, bool kInt8>
 int launch_warp(const moe::gemm::WarpParams& wp, int grid, cudaStream_t stream) {
   constexpr size_t smem = moe::gemm::warp_smem_bytes<kWarps>();
   static_assert(2 * (smem + 1024) <= 233472, "two warp-MMA CTAs per SM");
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_warp_kernel<kWarps>,
+    attr_err = cudaFuncSetAttribute(moe::gemm::grouped_gemm_warp_kernel<kWarps, kInt8>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(warp gemm)");
-  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_warp_kernel<kWarps>, dim3(grid),
+  CUDA_TRY(launch_pdl(moe::gemm::grouped_gemm_warp_kernel<kWarps, kInt8>, dim3(grid),
                       dim3(moe::gemm::WarpConfig<kWarps>::kThreads), smem, stream, wp),
            "grouped_gemm_warp_kernel launch");
   return MOE_OK;
 }
 
-// The warp-MMA kernel over up to two FFN segments (16-bit weights, one K
-// range, no gathered rows, 16-bit outputs), two CTAs per SM. Tiles of 64
+// The warp-MMA kernel over up to two FFN segments (16-bit or int8 weights,
+// one K range, no gathered rows, 16-bit outputs), two CTAs per SM. Tiles of 64
 // weight rows (four MMA warps, eight stages) when even twice as many tiles as
 // 128-row ones leave CTA slots free -- a decode step's few tiles then use
 // twice the SMs with the same weight bytes in flight per tile (C2 T=1 layer
@@ -447,10 +447,12 @@ int run_gemm_warp(const SegSpec* specs_in, int nseg, const int64_t* avg_rows, in
   std::memset(&wp, 0, sizeof(wp));
   wp.nt = nt;
   int64_t tiles = 0;
+  bool any_i8 = false;
   for (int i = 0; i < nseg; ++i) {
     SegSpec spec = specs_in[i];
-    CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
-              "the warp-MMA kernel takes 16-bit weights, one K range, no gathered rows, 16-bit outputs");
+    CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows,
+              "the warp-MMA kernel takes one K range, no gathered rows, 16-bit outputs");
+    any_i8 |= spec.b_dtype == MOE_DT_I8;
     spec.mma_n = 16 * warps;
     spec.a_box_rows = nt;
     spec.b_box_rows = 0;  // half gate, half up rows, or all rows
@@ -469,8 +471,11 @@ int run_gemm_warp(const SegSpec* specs_in, int nseg, const int64_t* avg_rows, in
   wp.p.status = status;
   const int64_t grid = tiles < slots ? tiles : slots;
   if (grid <= 0) return MOE_OK;
-  return warps == 8 ? launch_warp<8>(wp, static_cast<int>(grid), stream)
-                    : launch_warp<4>(wp, static_cast<int>(grid), stream);
+  if (any_i8)
+    return warps == 8 ? launch_warp<8, true>(wp, static_cast<int>(grid), stream)
+                      : launch_warp<4, true>(wp, static_cast<int>(grid), stream);
+  return warps == 8 ? launch_warp<8, false>(wp, static_cast<int>(grid), stream)
+                    : launch_warp<4, false>(wp, static_cast<int>(grid), stream);
 }
 
 // ---------------------------------------------------------------- streaming kernel
@@ -923,6 +928,10 @@ int moe_expert_ffn_part(int part, const void* xs, int act_dtype, int64_t R, int6
 // 123.5 us, T=128 141.8 -> 175.8 us.
 constexpr int64_t kStreamMaxAvgRows = 2;
 constexpr int64_t kStreamMaxSharedRows = 32;
+// AUTO takes the warp-MMA kernel for int8 weights with H or I beyond this
+// only for launches of at most kWarpI8WideMaxRows routed rows.
+constexpr int64_t kWarpI8MaxK = 4096;
+constexpr int64_t kWarpI8WideMaxRows = 8;
 
 // Where the routed down projection stores its rows: y, or scattered through
 // a table of (possibly peer) return buffers.
@@ -987,22 +996,27 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
   // Kernel choice per projection (every choice gives the same bits). AUTO,
   // for decode-sized batches (routed groups averaging at most
   // kStreamMaxAvgRows rows, a shared expert of at most kStreamMaxSharedRows):
-  // the warp-MMA kernel for both projections with 16-bit weights (C2 layer as
-  // a CUDA graph on B200, against the streaming gate/up + tiled down: T=1 81
-  // -> 71 us, T=4 137 -> 117 us, T=16 209 -> 190 us; slower from T=64 on),
-  // the streaming kernel for the gate/up projection with int8 weights; the
-  // tiled kernel otherwise -- and for an int8 down projection always, which
-  // the tiled kernel ran faster at every batch size measured (C2 T=1: 21 vs
-  // 33 us; T=16: 58 vs 89 us).
+  // the warp-MMA kernel for both projections (C2 layer as a CUDA graph on
+  // B200, against the streaming gate/up + tiled down: T=1 81 -> 71 us, T=4
+  // 137 -> 117 us, T=16 209 -> 190 us; slower from T=64 on; int8 below);
+  // the tiled (or CTA-pair) kernel otherwise.
   const int choice = g_ffn_kernel.load();
   const bool streamable = !gather_rows;
   CHECK_ARG(choice != MOE_FFN_KERNEL_STREAM || streamable, "the streaming kernel does not take gathered rows");
   const bool small = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
-  const bool warpable = streamable && w_dtype != MOE_DT_I8;
-  CHECK_ARG(choice != MOE_FFN_KERNEL_WARP || warpable, "the warp-MMA kernel takes 16-bit weights and no gathered rows");
-  const bool warp_mma = choice == MOE_FFN_KERNEL_WARP || (choice == MOE_FFN_KERNEL_AUTO && warpable && small);
-  const bool stream1 = !warp_mma && (choice == MOE_FFN_KERNEL_STREAM ||
-                                     (choice == MOE_FFN_KERNEL_AUTO && streamable && small));
+  const bool warpable = streamable;
+  CHECK_ARG(choice != MOE_FFN_KERNEL_WARP || warpable, "the warp-MMA kernel takes no gathered rows");
+  // int8: an int8 stage holds half the weight bytes of a 16-bit one. C3
+  // (H 2048, I 1408) layer graphs, warp-MMA / tiled / streaming, us: T=1 81 /
+  // 117 / 105, T=16 254 / 268 / 298, T=32 329 / 313 / 366; C5 (H 7168, I
+  // 2048): T=1 283 / 295 / 344, T=2 408 / 385 / 462, T=8 1244 / 1051 / 1387.
+  // So with K beyond kWarpI8MaxK the warp-MMA kernel only for about one
+  // token's rows, and the streaming kernel, slower than one of the others at
+  // every point measured, only when forced.
+  const bool wide_i8 = w_dtype == MOE_DT_I8 && (H > kWarpI8MaxK || I > kWarpI8MaxK);
+  const bool warp_auto = small && (!wide_i8 || R <= kWarpI8WideMaxRows);
+  const bool warp_mma = choice == MOE_FFN_KERNEL_WARP || (choice == MOE_FFN_KERNEL_AUTO && warpable && warp_auto);
+  const bool stream1 = !warp_mma && choice == MOE_FFN_KERNEL_STREAM;
   const bool stream2 = choice == MOE_FFN_KERNEL_STREAM;
   // row tile per segment for the streaming kernel: about the rows a group
   // holds (routed: the average per group; shared: all of its rows), in [32, 256]

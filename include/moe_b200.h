@@ -68,18 +68,18 @@ extern "C" {
  *   MOE_FFN_KERNEL_STREAM  one or two blocks of 128 weight rows x a tile of
  *                          32 to 256 token rows, up to 12 stages of weights
  *                          in flight per SM (decode-sized groups);
- *   MOE_FFN_KERNEL_WARP    128 weight rows x up to 32 token rows per tile,
- *                          eight warps per CTA each running its own chain of
- *                          warp-level MMAs (mma.sync) on TMA-staged operands,
- *                          two CTAs per SM (decode-sized groups); 16-bit
- *                          weights only;
+ *   MOE_FFN_KERNEL_WARP    64 or 128 weight rows x 8 to 32 token rows per
+ *                          tile, each warp of the CTA running its own chain
+ *                          of warp-level MMAs (mma.sync) on TMA-staged
+ *                          operands, two CTAs per SM (decode-sized groups);
+ *                          int8 weights are converted in registers;
  *   MOE_FFN_KERNEL_AUTO    (default) when the routed groups average at most
  *                          2 rows and the shared expert has at most 32: WARP
- *                          for both projections (16-bit weights), or STREAM
- *                          for the gate/up projection (int8 weights); else
- *                          PAIR when its 256-row tiles compute no more rows
- *                          than 128-row tiles would (16-bit weights), else
- *                          TILED.
+ *                          for both projections (int8 weights with H or I
+ *                          above 4096: only for at most 8 routed rows);
+ *                          otherwise PAIR when its 256-row tiles compute no
+ *                          more rows than 128-row tiles would (16-bit
+ *                          weights), else TILED. STREAM only when forced.
  * Every kernel gives every row the same bits (same k-block order; the tensor
  * cores' result depends neither on operand orientation nor on the tile or
  * CTA-group shape), so the choice changes speed only. Process-wide; returns the previous choice, or -1 for an

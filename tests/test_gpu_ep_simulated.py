@@ -71,8 +71,6 @@ def test_simulated_peer_ep_is_byte_exact_vs_one_gpu(weights: LayerWeights, world
               "ep stream / 1-GPU tiled": (L.FFN_KERNEL_STREAM, L.FFN_KERNEL_TILED),
               "ep tiled / 1-GPU stream": (L.FFN_KERNEL_TILED, L.FFN_KERNEL_STREAM),
               "ep warp / 1-GPU tiled": (L.FFN_KERNEL_WARP, L.FFN_KERNEL_TILED)}[kernels]
-    if quant and kernels == "ep warp / 1-GPU tiled":
-        pytest.skip("the warp-MMA kernel takes 16-bit weights")
     g = torch.Generator(device="cuda").manual_seed(4000 + world * 10 + len(set(tokens)))
     xs = [randn((t, H), g, 1.0) for t in tokens]
     ws = StackedExpertWeights(lw.gate, lw.up, lw.down)

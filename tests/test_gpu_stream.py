@@ -123,8 +123,9 @@ def test_stream_layer_equals_tiled(c2: LayerWeights, t: int, quant: bool) -> Non
         assert torch.equal(a, b), f"T={t}: max |diff| {(a.float() - b.float()).abs().max().item()}"
 
 
-def test_stream_is_the_automatic_choice_for_decode(c2: LayerWeights) -> None:
-    """AUTO gives the same bits as either forced kernel at a decode size."""
+def test_automatic_choice_at_decode_gives_the_forced_kernels_bits(c2: LayerWeights) -> None:
+    """AUTO (the warp-MMA kernel at this decode size) gives the same bits as
+    the forced tiled and streaming kernels."""
     ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
     x = randn((4, 2048), torch.Generator(device="cuda").manual_seed(5), 1.0)
     fwd = lambda: moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6), shared=sh).out  # noqa: E731
@@ -214,19 +215,30 @@ def test_warp_grouped_matmul_equals_tiled(dtype, sizes, n, k) -> None:
     assert torch.equal(a, b), f"max |diff| {(a.float() - b.float()).abs().max().item()}"
 
 
-def test_warp_kernel_rejects_int8_weights(c2: LayerWeights) -> None:
-    ws = quantize_stacked_weights(StackedExpertWeights(c2.gate, c2.up, c2.down), scale_dtype=torch.bfloat16)
-    x = randn((4, 2048), torch.Generator(device="cuda").manual_seed(8), 1.0)
-    with ffn_kernel(L.FFN_KERNEL_WARP), pytest.raises(ValueError, match="16-bit weights"):
-        moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6))
+@pytest.mark.parametrize("scale_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize(("sizes", "n", "k"), GEMM_CASES)
+def test_warp_int8_grouped_matmul_equals_tiled(scale_dtype, sizes, n, k) -> None:
+    """int8 weights on the warp-MMA kernel (each warp converts its own rows
+    into the MMA operand registers, scales applied in the epilogue): the
+    tiled kernel's bits."""
+    g = torch.Generator(device="cuda").manual_seed(36)
+    sched = build_tile_schedule(torch.tensor(sizes, device=DEV), block_m=16)
+    x = randn((sum(sizes), k), g, 1.0)
+    q = quantize_per_channel_int8(randn((len(sizes), n, k), g, k ** -0.5, torch.float32), scale_dtype=scale_dtype)
+    a, b = _warp_vs_tiled(lambda: grouped_matmul_int8(x, q, sched))
+    assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("t", [1, 7, 16, 64, 300])
-def test_warp_layer_equals_tiled(c2: LayerWeights, t: int) -> None:
+@pytest.mark.parametrize("quant", [False, True])
+def test_warp_layer_equals_tiled(c2: LayerWeights, t: int, quant: bool) -> None:
     """The whole C2 layer with both FFN projections on the warp-MMA kernel
     (SwiGLU pairs exchanging accumulators through shared memory, the shared
-    expert as a dense segment): the tiled kernel's bits, uniform and Zipf."""
+    expert as a dense segment; int8 routed experts beside the bf16 shared
+    expert in one launch): the tiled kernel's bits, uniform and Zipf."""
     ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
+    if quant:
+        ws = quantize_stacked_weights(ws, scale_dtype=torch.bfloat16)
     x = randn((t, 2048), torch.Generator(device="cuda").manual_seed(970 + t), 1.0)
     for bias in (None, -1.2 * torch.log(torch.arange(64, dtype=torch.float32, device=DEV) + 1.0)):
         a, b = _warp_vs_tiled(lambda: moe_layer_forward(x, c2.router, ws, RouterConfig(top_k=6), shared=sh,
