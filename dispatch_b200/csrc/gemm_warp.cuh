@@ -221,15 +221,22 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
         decode_tile(c, p, t, tl, nt_tile);
         const Segment& Sg = p.seg[tl.seg];
         const int n0 = tl.n_tile * out_cols_per_tile(Sg);
-        for (int kb = tl.kb0; kb < tl.kb1; ++kb) {
+        const bool q8 = kInt8 && Sg.b_int8;
+        // int8 rows are half as wide: a stage then carries two k-blocks (the
+        // second fully beyond K is zero-filled and not computed)
+        const int kpb = (q8 && 2 * nt_tile * BK * 2 <= static_cast<int>(kWXBytes)) ? 2 : 1;
+        for (int kb = tl.kb0; kb < tl.kb1; kb += kpb) {
           if (!wait_parity_bounded(&c.empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          const bool q8 = kInt8 && Sg.b_int8;
-          const uint32_t w_bytes = q8 ? kWWBytes / 2 : kWWBytes;  // int8: 64-byte rows
-          mbar_arrive_expect_tx(&c.full[stage], w_bytes + static_cast<uint32_t>(nt_tile) * BK * 2);
-          uint8_t* w_dst = sW + stage * kWWBytes;
-          tma_load_2d(sX + stage * kWXBytes, &Sg.map_a, &c.full[stage], kb * BK, tl.row0);
-          tma_load_3d(w_dst, &Sg.map_b0, &c.full[stage], kb * BK, n0, tl.widx);
-          if (Sg.swiglu) tma_load_3d(w_dst + w_bytes / 2, &Sg.map_b1, &c.full[stage], kb * BK, n0, tl.widx);
+          const uint32_t w_bytes = q8 ? kWWBytes / 2 : kWWBytes;  // per k-block; int8: 64-byte rows
+          const uint32_t x_bytes = static_cast<uint32_t>(nt_tile) * BK * 2;
+          mbar_arrive_expect_tx(&c.full[stage], static_cast<uint32_t>(kpb) * (w_bytes + x_bytes));
+          for (int j = 0; j < kpb; ++j) {
+            uint8_t* w_dst = sW + stage * kWWBytes + j * w_bytes;
+            tma_load_2d(sX + stage * kWXBytes + j * x_bytes, &Sg.map_a, &c.full[stage], (kb + j) * BK, tl.row0);
+            tma_load_3d(w_dst, &Sg.map_b0, &c.full[stage], (kb + j) * BK, n0, tl.widx);
+            if (Sg.swiglu)
+              tma_load_3d(w_dst + w_bytes / 2, &Sg.map_b1, &c.full[stage], (kb + j) * BK, n0, tl.widx);
+          }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -271,15 +278,17 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-      for (int kb = tl.kb0; ok && kb < tl.kb1; ++kb) {
+      const int kpb = (q8 && 2 * nt_tile * BK * 2 <= static_cast<int>(kWXBytes)) ? 2 : 1;
+      for (int kb = tl.kb0; ok && kb < tl.kb1; kb += kpb) {
         // every lane waits (its own acquire of the TMA bytes); the warp then
         // agrees on the outcome so that it leaves the loop together
         const bool got = wait_parity_bounded(&c.full[stage], phase, abort_flag, p.status);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         const uint32_t wbase = smem_u32(sW + stage * kWWBytes);
-        const uint32_t xbase = smem_u32(sX + stage * kWXBytes);
+        for (int j = 0; j < kpb && kb + j < tl.kb1; ++j) {
+        const uint32_t xbase = smem_u32(sX + stage * kWXBytes) + static_cast<uint32_t>(j * nt_tile * BK * 2);
         // int8: this thread's bytes (rows g and g + 8, k = 2tq.. and 8 + 2tq..)
-        const uint8_t* q0 = sW + stage * kWWBytes + (16 * w + g) * BK + 2 * tq;
+        const uint8_t* q0 = sW + stage * kWWBytes + j * (kWWBytes / 2) + (16 * w + g) * BK + 2 * tq;
 #pragma unroll
         for (int s = 0; s < BK / 16; ++s) {
           uint32_t a[4];
@@ -301,6 +310,7 @@ __global__ void __launch_bounds__(WarpConfig<kWarps>::kThreads)
               if (2 * jj + 1 < nt) mma_16816(acc[2 * jj + 1], a, b[2], b[3], p.in_f16);
             }
           }
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&c.empty[stage]);
