@@ -365,7 +365,8 @@ int launch_pair(const moe::gemm::Params& p, int grid, cudaStream_t stream) {
 }
 
 // The CTA-pair kernel over up to two FFN segments (16-bit weights, one K
-// range, no gathered rows, 16-bit outputs): tiles of 256 rows x 256 columns.
+// range, no gathered rows, 16-bit outputs): tiles of 256 weight rows x up to
+// 256 token rows.
 int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* status, cudaStream_t stream) {
   int sms = 0;
   int rc = device_info(&sms);
@@ -378,7 +379,9 @@ int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* sta
     CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
               "the CTA-pair kernel takes 16-bit weights, one K range, 16-bit outputs");
     spec.mma_n = 2 * moe::gemm::BM;
-    spec.b_box_rows = moe::gemm::BM;  // each CTA loads 128 weight rows
+    // each CTA loads 128 weight rows: 64 gate + 64 up rows, or 128 plain rows;
+    // and its half of the tile's token rows in boxes of 16
+    spec.b_box_rows = spec.swiglu ? moe::gemm::BM / 2 : moe::gemm::BM;
     rc = check_seg(spec, act_dtype);
     if (rc) return rc;
     rc = fill_segment(&p.seg[i], spec, act_dtype);
@@ -1027,27 +1030,22 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     if (R > 0) nts[i++] = row_tile((R + G - 1) / G);
     if (has_shared) nts[i++] = row_tile(T_shared);
   }
-  // The CTA-pair kernel (16-bit weights) when its 256-row tiles compute no
-  // more rows than the tiled kernel's 128-row tiles (within 5%), judged from
-  // the average group: both kernels ran at about the same tensor rate per
-  // computed row on B200, the pair kernel some 5-13% faster (C2 gate/up:
-  // T=2048 237 -> 210 us, both computing 256 rows for groups of ~192), so the
-  // rows a tile shape wastes decide (T=4096, groups of ~384: 376 vs 405 us).
+  // The CTA-pair kernel (16-bit weights) for groups of prefill size whose last
+  // 256-row tile is not nearly empty, judged from the average group. Both
+  // kernels are bound by shared-memory traffic per k-block, which a tile pays
+  // whatever its row count (B200, C2 T=4096, per-CTA cycle counters): 771
+  // cycles per k-block on one SM for a 128-row tile, 661 per SM of a CTA pair
+  // for up to 256 token rows; so the pair kernel gains where its tiles are
+  // full and loses where a group's last tile holds a few rows. C2 layer
+  // graphs, tiled / pair, us (average group r): T=1024 (96) 287 / 309,
+  // T=2048 (192) 426 / 405, T=3072 (288) 593 / 620, T=4096 (384) 715-736 /
+  // 677-717, T=6144 (576) 1016 / 1026, T=8192 (768) 1290 / 1239.
   const bool pairable = streamable && w_dtype != MOE_DT_I8;
   CHECK_ARG(choice != MOE_FFN_KERNEL_PAIR || pairable, "the CTA-pair kernel takes 16-bit weights and no gathered rows");
-  auto rounded = [](int64_t rows, int64_t tile) { return (rows + tile - 1) / tile * tile; };
-  int64_t rows128 = 0, rows256 = 0;  // rows computed by 128- and 256-row tiles
-  if (R > 0) {
-    const int64_t avg = (R + G - 1) / G;
-    rows128 += G * rounded(avg, 128);
-    rows256 += G * rounded(avg, 256);
-  }
-  if (has_shared) {
-    rows128 += rounded(T_shared, 128);
-    rows256 += rounded(T_shared, 256);
-  }
-  const bool pair = choice == MOE_FFN_KERNEL_PAIR ||
-                    (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && rows256 * 20 <= rows128 * 21);
+  const int64_t avg_group = R > 0 ? (R + G - 1) / G : T_shared;
+  const int64_t tail = avg_group % 256;
+  const bool pair_auto = avg_group >= 160 && (tail == 0 || tail >= 96);
+  const bool pair = choice == MOE_FFN_KERNEL_PAIR || (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && pair_auto);
   int64_t avg_rows[2] = {1, 1};  // rows of the average group per segment (warp-MMA token tile)
   {
     int i = 0;
