@@ -62,9 +62,10 @@ extern "C" {
  * moe_layer_forward) launch:
  *   MOE_FFN_KERNEL_TILED   128 token rows x 256 weight columns per tile
  *                          (prefill-sized groups);
- *   MOE_FFN_KERNEL_PAIR    256 token rows x 256 weight columns per tile on a
- *                          pair of SMs (tcgen05 cta_group::2, each SM stages
- *                          half of both operands); 16-bit weights only;
+ *   MOE_FFN_KERNEL_PAIR    256 weight rows x up to 256 token rows (a
+ *                          multiple of 32) per tile on a pair of SMs (tcgen05
+ *                          cta_group::2, each SM stages 128 weight rows and
+ *                          half of the token rows); 16-bit weights only;
  *   MOE_FFN_KERNEL_STREAM  one or two blocks of 128 weight rows x a tile of
  *                          32 to 256 token rows, up to 12 stages of weights
  *                          in flight per SM (decode-sized groups);
@@ -77,9 +78,10 @@ extern "C" {
  *                          2 rows and the shared expert has at most 32: WARP
  *                          for both projections (int8 weights with H or I
  *                          above 4096: only for at most 8 routed rows);
- *                          otherwise PAIR when its 256-row tiles compute no
- *                          more rows than 128-row tiles would (16-bit
- *                          weights), else TILED. STREAM only when forced.
+ *                          otherwise PAIR (16-bit weights) when the average
+ *                          group has at least 160 rows and its last 256-row
+ *                          tile is empty or holds at least 96 rows, else
+ *                          TILED. STREAM only when forced.
  * Every kernel gives every row the same bits (same k-block order; the tensor
  * cores' result depends neither on operand orientation nor on the tile or
  * CTA-group shape), so the choice changes speed only. Process-wide; returns the previous choice, or -1 for an
