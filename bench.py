@@ -767,11 +767,15 @@ def int8_layer_line(t: int, peaks: dict, dev, stream) -> dict:
             "checked": checked}
 
 
-# DRAM bytes (read + write) of one gate/up launch on the C2 T=4096 step, from
-# an ncu capture of this kernel (dram__bytes_read.sum + dram__bytes_write.sum).
-GATEUP_TRAFFIC_C2 = 879.5e6 + 68.4e6
-GATEUP_TRAFFIC_SOURCE = ("ncu capture of this kernel on the C2 T=4096 step (dram__bytes_read.sum + "
-                         "dram__bytes_write.sum), profiles/grouped_gemm_c2_t4096.md; not measured in this run")
+# DRAM bytes (read + write) of one gate/up launch, per (workload, T, kernel),
+# from ncu captures of that kernel on that step (dram__bytes_read.sum +
+# dram__bytes_write.sum).
+GATEUP_TRAFFIC = {
+    ("c2", 4096, "grouped_gemm_kernel<bf16>"): 879.5e6 + 68.4e6,
+    ("c2", 4096, "grouped_gemm_pair_kernel"): 911.25e6 + 74.97e6,
+}
+GATEUP_TRAFFIC_SOURCE = ("ncu capture of this kernel on this step (dram__bytes_read.sum + dram__bytes_write.sum), "
+                         "profiles/; not measured in this run")
 
 
 def gateup_roofline(wl: Workload, x, ws, sh, res, peaks, peak_kind, dev, stream) -> dict:
@@ -811,14 +815,16 @@ def gateup_roofline(wl: Workload, x, ws, sh, res, peaks, peak_kind, dev, stream)
     f1 = wl.gateup_flops(r, t)
     achieved = f1 / (ms1 * 1e-3) / 1e12
     f2 = wl.down_flops(r, t)
-    measured = wl.name == "c2" and t == 4096 and not quant
-    traffic = GATEUP_TRAFFIC_C2 if measured else None
-    kernel = "grouped_gemm_kernel<int8> gate/up + SwiGLU" if quant else "grouped_gemm_kernel<bf16> gate/up + SwiGLU"
-    return {"kernel": kernel + " (routed + shared)", "bound": "tensor",
+    # the kernel the automatic choice launches for this call
+    choice = lib.moe_ffn_kernel_auto(r, wl.E, t, wl.H, wl.I, L.DT_I8 if quant else L.DT_BF16)
+    kernel = {L.FFN_KERNEL_PAIR: "grouped_gemm_pair_kernel", L.FFN_KERNEL_WARP: "grouped_gemm_warp_kernel"}.get(
+        choice, "grouped_gemm_kernel<int8>" if quant else "grouped_gemm_kernel<bf16>")
+    traffic = GATEUP_TRAFFIC.get((wl.name, t, kernel))
+    return {"kernel": kernel + " gate/up + SwiGLU (routed + shared)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 4), "peak_kind": f"{peak_kind} burst",
             "launch_ms": round(ms1, 4), "flops_per_launch": f1, "traffic": traffic,
-            "traffic_source": GATEUP_TRAFFIC_SOURCE if measured else "not captured for this config",
+            "traffic_source": GATEUP_TRAFFIC_SOURCE if traffic else "not captured for this config and kernel",
             "down_gemm": {"launch_ms": round(ms2, 4), "achieved": round(f2 / (ms2 * 1e-3) / 1e12, 1)}}
 
 

@@ -58,6 +58,7 @@ class MoeLayerDesc(ctypes.Structure):
 _SIGNATURES = {
     "moe_abi_version": ([], _i32),
     "moe_set_ffn_kernel": ([_i32], _i32),
+    "moe_ffn_kernel_auto": ([_i64, _i64, _i64, _i64, _i64, _i32], _i32),
     "moe_status_string": ([_i32], ctypes.c_char_p),
     "moe_last_error": ([], ctypes.c_char_p),
     "moe_device_sm_count": ([], _i32),

@@ -611,6 +611,14 @@ int moe_set_ffn_kernel(int choice) {
   return g_ffn_kernel.exchange(choice);
 }
 
+static int ffn_auto_kernel(int64_t R, int64_t G, int64_t T_shared, int64_t H, int64_t I, int w_dtype,
+                           bool gather);
+
+int moe_ffn_kernel_auto(int64_t R, int64_t G, int64_t T_shared, int64_t H, int64_t I, int w_dtype) {
+  if (R < 0 || G < 1 || T_shared < 0 || H < 0 || I < 0) return -1;
+  return ffn_auto_kernel(R, G, T_shared, H, I, w_dtype, false);
+}
+
 const char* moe_status_string(int code) {
   switch (code) {
     case MOE_OK: return "ok";
@@ -945,6 +953,43 @@ struct RoutedOut {
   int64_t table_rows = 0;
 };
 
+// The kernel MOE_FFN_KERNEL_AUTO runs for one expert-FFN call (both
+// projections): R routed rows in G groups, a shared expert over T_shared rows
+// (0: none), hidden size H, intermediate size I, weight dtype w_dtype.
+//  - Decode-sized batches (routed groups averaging at most kStreamMaxAvgRows
+//    rows, a shared expert of at most kStreamMaxSharedRows): the warp-MMA
+//    kernel (C2 layer as a CUDA graph on B200, against the streaming gate/up
+//    + tiled down: T=1 81 -> 71 us, T=4 137 -> 117 us, T=16 209 -> 190 us;
+//    slower from T=64 on). int8: an int8 stage holds half the weight bytes of
+//    a 16-bit one. C3 (H 2048, I 1408) layer graphs, warp-MMA / tiled /
+//    streaming, us: T=1 81 / 117 / 105, T=16 254 / 268 / 298, T=32 329 / 313
+//    / 366; C5 (H 7168, I 2048): T=1 283 / 295 / 344, T=2 408 / 385 / 462,
+//    T=8 1244 / 1051 / 1387. So with K beyond kWarpI8MaxK the warp-MMA kernel
+//    only for about one token's rows; the streaming kernel, slower than one
+//    of the others at every point measured, never.
+//  - The CTA-pair kernel (16-bit weights) for groups of prefill size whose
+//    last 256-row tile is not nearly empty, judged from the average group.
+//    Both tcgen05 kernels are bound by shared-memory traffic per k-block,
+//    which a tile pays whatever its row count (B200, C2 T=4096, per-CTA cycle
+//    counters): 771 cycles per k-block on one SM for a 128-row tile, 661 per
+//    SM of a CTA pair for up to 256 token rows; so the pair kernel gains
+//    where its tiles are full and loses where a group's last tile holds a few
+//    rows. C2 layer graphs, tiled / pair, us (average group r): T=1024 (96)
+//    287 / 309, T=2048 (192) 426 / 405, T=3072 (288) 593 / 620, T=4096 (384)
+//    715-736 / 677-717, T=6144 (576) 1016 / 1026, T=8192 (768) 1290 / 1239.
+//  - Else the tiled kernel. Gathered rows (TMA tile::gather4) only run there.
+static int ffn_auto_kernel(int64_t R, int64_t G, int64_t T_shared, int64_t H, int64_t I, int w_dtype, bool gather) {
+  if (gather) return MOE_FFN_KERNEL_TILED;
+  const bool has_shared = T_shared > 0;
+  const bool small = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
+  const bool wide_i8 = w_dtype == MOE_DT_I8 && (H > kWarpI8MaxK || I > kWarpI8MaxK);
+  if (small && (!wide_i8 || R <= kWarpI8WideMaxRows)) return MOE_FFN_KERNEL_WARP;
+  const int64_t avg_group = R > 0 ? (R + G - 1) / G : T_shared;
+  const int64_t tail = avg_group % 256;
+  if (w_dtype != MOE_DT_I8 && avg_group >= 160 && (tail == 0 || tail >= 96)) return MOE_FFN_KERNEL_PAIR;
+  return MOE_FFN_KERNEL_TILED;
+}
+
 static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t H, const int32_t* offsets, int64_t G,
                     int64_t E, const int64_t* gather_rows, int64_t gather_src_rows, int64_t I, const void* gate,
                     const void* up, const void* down, int w_dtype, const void* gate_scale, const void* up_scale,
@@ -996,31 +1041,21 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     ++n;
   }
   if (n == 0) return MOE_OK;
-  // Kernel choice per projection (every choice gives the same bits). AUTO,
-  // for decode-sized batches (routed groups averaging at most
-  // kStreamMaxAvgRows rows, a shared expert of at most kStreamMaxSharedRows):
-  // the warp-MMA kernel for both projections (C2 layer as a CUDA graph on
-  // B200, against the streaming gate/up + tiled down: T=1 81 -> 71 us, T=4
-  // 137 -> 117 us, T=16 209 -> 190 us; slower from T=64 on; int8 below);
-  // the tiled (or CTA-pair) kernel otherwise.
+  // Kernel choice (every choice gives the same bits): the forced one, or
+  // ffn_auto_kernel's; STREAM runs the streaming kernel for both projections.
   const int choice = g_ffn_kernel.load();
   const bool streamable = !gather_rows;
   CHECK_ARG(choice != MOE_FFN_KERNEL_STREAM || streamable, "the streaming kernel does not take gathered rows");
-  const bool small = (R == 0 || R <= kStreamMaxAvgRows * G) && (!has_shared || T_shared <= kStreamMaxSharedRows);
-  const bool warpable = streamable;
-  CHECK_ARG(choice != MOE_FFN_KERNEL_WARP || warpable, "the warp-MMA kernel takes no gathered rows");
-  // int8: an int8 stage holds half the weight bytes of a 16-bit one. C3
-  // (H 2048, I 1408) layer graphs, warp-MMA / tiled / streaming, us: T=1 81 /
-  // 117 / 105, T=16 254 / 268 / 298, T=32 329 / 313 / 366; C5 (H 7168, I
-  // 2048): T=1 283 / 295 / 344, T=2 408 / 385 / 462, T=8 1244 / 1051 / 1387.
-  // So with K beyond kWarpI8MaxK the warp-MMA kernel only for about one
-  // token's rows, and the streaming kernel, slower than one of the others at
-  // every point measured, only when forced.
-  const bool wide_i8 = w_dtype == MOE_DT_I8 && (H > kWarpI8MaxK || I > kWarpI8MaxK);
-  const bool warp_auto = small && (!wide_i8 || R <= kWarpI8WideMaxRows);
-  const bool warp_mma = choice == MOE_FFN_KERNEL_WARP || (choice == MOE_FFN_KERNEL_AUTO && warpable && warp_auto);
-  const bool stream1 = !warp_mma && choice == MOE_FFN_KERNEL_STREAM;
-  const bool stream2 = choice == MOE_FFN_KERNEL_STREAM;
+  CHECK_ARG(choice != MOE_FFN_KERNEL_WARP || streamable, "the warp-MMA kernel takes no gathered rows");
+  CHECK_ARG(choice != MOE_FFN_KERNEL_PAIR || (streamable && w_dtype != MOE_DT_I8),
+            "the CTA-pair kernel takes 16-bit weights and no gathered rows");
+  const int pick = choice == MOE_FFN_KERNEL_AUTO
+                       ? ffn_auto_kernel(R, G, has_shared ? T_shared : 0, H, I, w_dtype, gather_rows != nullptr)
+                       : choice;
+  const bool warp_mma = pick == MOE_FFN_KERNEL_WARP;
+  const bool stream1 = pick == MOE_FFN_KERNEL_STREAM;
+  const bool stream2 = pick == MOE_FFN_KERNEL_STREAM;
+  const bool pair = pick == MOE_FFN_KERNEL_PAIR;
   // row tile per segment for the streaming kernel: about the rows a group
   // holds (routed: the average per group; shared: all of its rows), in [32, 256]
   auto row_tile = [](int64_t rows) { return rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; };
@@ -1030,22 +1065,6 @@ static int ffn_impl(int part, const void* xs, int act_dtype, int64_t R, int64_t 
     if (R > 0) nts[i++] = row_tile((R + G - 1) / G);
     if (has_shared) nts[i++] = row_tile(T_shared);
   }
-  // The CTA-pair kernel (16-bit weights) for groups of prefill size whose last
-  // 256-row tile is not nearly empty, judged from the average group. Both
-  // kernels are bound by shared-memory traffic per k-block, which a tile pays
-  // whatever its row count (B200, C2 T=4096, per-CTA cycle counters): 771
-  // cycles per k-block on one SM for a 128-row tile, 661 per SM of a CTA pair
-  // for up to 256 token rows; so the pair kernel gains where its tiles are
-  // full and loses where a group's last tile holds a few rows. C2 layer
-  // graphs, tiled / pair, us (average group r): T=1024 (96) 287 / 309,
-  // T=2048 (192) 426 / 405, T=3072 (288) 593 / 620, T=4096 (384) 715-736 /
-  // 677-717, T=6144 (576) 1016 / 1026, T=8192 (768) 1290 / 1239.
-  const bool pairable = streamable && w_dtype != MOE_DT_I8;
-  CHECK_ARG(choice != MOE_FFN_KERNEL_PAIR || pairable, "the CTA-pair kernel takes 16-bit weights and no gathered rows");
-  const int64_t avg_group = R > 0 ? (R + G - 1) / G : T_shared;
-  const int64_t tail = avg_group % 256;
-  const bool pair_auto = avg_group >= 160 && (tail == 0 || tail >= 96);
-  const bool pair = choice == MOE_FFN_KERNEL_PAIR || (choice == MOE_FFN_KERNEL_AUTO && pairable && !stream1 && pair_auto);
   int64_t avg_rows[2] = {1, 1};  // rows of the average group per segment (warp-MMA token tile)
   {
     int i = 0;

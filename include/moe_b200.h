@@ -95,6 +95,17 @@ extern "C" {
 #define MOE_FFN_KERNEL_WARP 4
 int moe_set_ffn_kernel(int choice);
 
+/*
+ * The kernel (MOE_FFN_KERNEL_WARP, _PAIR or _TILED) that AUTO runs for an
+ * expert-FFN call with R routed rows in G groups (experts, or (rank, expert)
+ * groups), a shared expert over T_shared rows (0: none), hidden size H,
+ * intermediate size I and weight dtype w_dtype (MOE_DT_BF16 / _F16 / _I8),
+ * without gathered rows. Host-only (no device, no allocation); for logs and
+ * benchmarks that name the kernel they time. -1 for a negative size or G < 1.
+ * No reference counterpart.
+ */
+int moe_ffn_kernel_auto(int64_t R, int64_t G, int64_t T_shared, int64_t H, int64_t I, int w_dtype);
+
 /* router modes */
 #define MOE_ROUTER_SOFTMAX 0        /* softmax top-k (optionally renormalised) */
 #define MOE_ROUTER_SIGMOID_GROUP 1  /* DeepSeek-V3 group-limited sigmoid top-k */

@@ -65,6 +65,34 @@ def test_workspace_helpers_are_pure_host_arithmetic() -> None:
     assert lib.moe_layer_workspace_bytes(ctypes.byref(d)) > 2 * 4096 * 6 * 2048 * 2
 
 
+@pytest.mark.parametrize(("t", "w_dtype", "expect"), [
+    (1, L.DT_BF16, L.FFN_KERNEL_WARP),     # decode: routed groups of ~0.1 rows, shared expert of 1
+    (16, L.DT_BF16, L.FFN_KERNEL_WARP),    # 96 routed rows over 64 experts, shared 16
+    (64, L.DT_BF16, L.FFN_KERNEL_TILED),   # routed groups of 6 rows: past the decode rule
+    (1024, L.DT_BF16, L.FFN_KERNEL_TILED),  # groups of 96
+    (2048, L.DT_BF16, L.FFN_KERNEL_PAIR),  # groups of 192: one well-filled pair tile
+    (3072, L.DT_BF16, L.FFN_KERNEL_TILED),  # groups of 288: a last pair tile of 32 rows
+    (4096, L.DT_BF16, L.FFN_KERNEL_PAIR),  # groups of 384
+    (4096, L.DT_I8, L.FFN_KERNEL_TILED),   # int8 weights: the pair kernel takes 16-bit ones
+    (1, L.DT_I8, L.FFN_KERNEL_WARP),
+])
+def test_automatic_kernel_choice_on_c2_shapes(t: int, w_dtype: int, expect: int) -> None:
+    """The host-only query names the kernel AUTO launches for the C2 layer
+    (H 2048, 64 experts top-6, I 1408, one shared expert over all T rows)."""
+    assert L.lib().moe_ffn_kernel_auto(t * 6, 64, t, 2048, 1408, w_dtype) == expect
+
+
+def test_automatic_kernel_choice_limits_wide_int8_decode() -> None:
+    """int8 with K above 4096 (the C5 shapes) keeps the warp-MMA kernel only
+    for about one token's routed rows; bad sizes answer -1."""
+    lib = L.lib()
+    assert lib.moe_ffn_kernel_auto(8, 256, 1, 7168, 2048, L.DT_I8) == L.FFN_KERNEL_WARP
+    assert lib.moe_ffn_kernel_auto(16, 256, 2, 7168, 2048, L.DT_I8) == L.FFN_KERNEL_TILED
+    assert lib.moe_ffn_kernel_auto(16, 256, 2, 7168, 2048, L.DT_BF16) == L.FFN_KERNEL_WARP
+    assert lib.moe_ffn_kernel_auto(-1, 64, 0, 2048, 1408, L.DT_BF16) == -1
+    assert lib.moe_ffn_kernel_auto(6, 0, 0, 2048, 1408, L.DT_BF16) == -1
+
+
 def test_python_ops_refuse_cpu_tensors() -> None:
     from dispatch_b200.kernels.grouped_gemm import grouped_matmul
     from dispatch_b200.kernels.grouping import group_tokens_by_expert
