@@ -1,15 +1,14 @@
 // Warp-MMA weight streaming for decode-sized groups (a few token rows per
 // expert).
 //
-// The tcgen05 kernels issue every MMA of a CTA from one thread, and a chain of
-// dependent tcgen05 MMAs into one accumulator runs at one MMA every few
-// hundred cycles whatever its width: with one or two token rows per expert
-// that, not HBM, bounds a decode step (C2 T=16: both FFN launches read their
-// weights at ~4.75 TB/s, against 6.9 TB/s for the same TMA boxes streamed
-// with no math). Here eight warps per CTA each run their own short chain of
-// warp-level MMAs (mma.sync m16n8k16: 16 weight rows x 8 token rows x 16 K)
-// on operands that TMA stages in shared memory, so a CTA keeps eight chains
-// in flight and an SM two CTAs.
+// With one or two token rows per expert the tcgen05 kernels, which issue every
+// MMA of a CTA from one thread, read their weights well below HBM speed (C2
+// T=16: both FFN launches at ~4.75 TB/s, against 6.9 TB/s for the same TMA
+// boxes streamed with no math). Here eight (or four) warps per CTA each run
+// their own short chain of warp-level MMAs (mma.sync m16n8k16: 16 weight rows
+// x 8 token rows x 16 K) on operands that TMA stages in shared memory, so a
+// CTA keeps that many chains in flight and an SM two CTAs; the same launches
+// read at 5.7-5.9 TB/s.
 //
 // Bits: an m16n8k16 MMA chain walked over K in order, 16 at a time, with f32
 // accumulation gives the same f32 values as the tcgen05 MMAs of the other
