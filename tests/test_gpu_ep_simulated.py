@@ -55,22 +55,27 @@ CASES = [
     (8, [1] * 8, True, False),  # decode: one token per rank
     (4, [200, 150, 100, 50], True, True),  # int8 experts
     (8, [33, 40, 0, 7, 128, 1, 64, 90], False, True),
+    (2, [2048, 2048], False, False),  # prefill: (rank, expert) groups of ~192 rows, CTA-pair tiles under AUTO
 ]
 
 
 @pytest.mark.parametrize("world,tokens,skew,quant", CASES)
 @pytest.mark.parametrize("kernels", ["auto", "ep stream / 1-GPU tiled", "ep tiled / 1-GPU stream",
-                                     "ep warp / 1-GPU tiled"])
+                                     "ep warp / 1-GPU tiled", "ep pair / 1-GPU tiled"])
 def test_simulated_peer_ep_is_byte_exact_vs_one_gpu(weights: LayerWeights, world, tokens, skew, quant,
                                                     kernels) -> None:
     """``kernels`` forces the FFN kernel of the EP ranks and of the 1-GPU
     reference to differ: the rows must match byte for byte whichever kernel
-    computed them, including the streaming kernel's scattered return stores."""
+    computed them, including the streaming and CTA-pair kernels' scattered
+    return stores."""
+    if quant and "pair" in kernels:
+        pytest.skip("the CTA-pair kernel takes 16-bit weights")
     lw = weights
     choice = {"auto": (L.FFN_KERNEL_AUTO, L.FFN_KERNEL_AUTO),
               "ep stream / 1-GPU tiled": (L.FFN_KERNEL_STREAM, L.FFN_KERNEL_TILED),
               "ep tiled / 1-GPU stream": (L.FFN_KERNEL_TILED, L.FFN_KERNEL_STREAM),
-              "ep warp / 1-GPU tiled": (L.FFN_KERNEL_WARP, L.FFN_KERNEL_TILED)}[kernels]
+              "ep warp / 1-GPU tiled": (L.FFN_KERNEL_WARP, L.FFN_KERNEL_TILED),
+              "ep pair / 1-GPU tiled": (L.FFN_KERNEL_PAIR, L.FFN_KERNEL_TILED)}[kernels]
     g = torch.Generator(device="cuda").manual_seed(4000 + world * 10 + len(set(tokens)))
     xs = [randn((t, H), g, 1.0) for t in tokens]
     ws = StackedExpertWeights(lw.gate, lw.up, lw.down)
