@@ -734,11 +734,15 @@ int moe_route(const void* x, int x_dtype, const void* router_w, int w_dtype, con
   const size_t smem = static_cast<size_t>(p.tb) * (p.E + (logits_in ? 0 : H)) * sizeof(float);
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(moe::route::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(moe::route::route_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(moe::route::route_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(moe::route::route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
   });
   const int64_t grid = (T + p.tb - 1) / p.tb;
-  CUDA_TRY(launch_pdl(moe::route::route_kernel, dim3(static_cast<unsigned>(grid)), dim3(moe::route::kThreads), smem,
-                      s, p),
+  // experts per lane in the selection: the fewest that cover E
+  auto kernel = p.E <= 64 ? moe::route::route_kernel<2> : p.E <= 128 ? moe::route::route_kernel<4>
+                                                                        : moe::route::route_kernel<8>;
+  CUDA_TRY(launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(moe::route::kThreads), smem, s, p),
            "route_kernel launch");
   return MOE_OK;
 }

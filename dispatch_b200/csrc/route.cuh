@@ -91,7 +91,12 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
+// J: experts per lane in the selection (32 * J >= E): the launch picks 2, 4 or
+// 8, so that a 64-expert router walks 2 slots per lane in each of its k
+// rounds instead of 8 (slots past E hold -inf and are never chosen, so J
+// changes the work, not the result).
+template <int J>
+__global__ void __launch_bounds__(kThreads, 4) route_kernel(const Params p) {
   pdl_trigger();
   pdl_wait();  // before the first global memory access
   extern __shared__ float smem_f[];
@@ -164,7 +169,6 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const Params p) {
     __syncthreads();
   }
 
-  constexpr int J = kMaxE / 32;
   for (int t = warp; t < ntok; t += kWarps) {
     const float* l = lg + t * E;
     float v[J];
