@@ -147,9 +147,10 @@ def _pair_vs_tiled(fn):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize(("sizes", "n", "k"), GEMM_CASES)
 def test_pair_grouped_matmul_equals_tiled(dtype, sizes, n, k) -> None:
-    """The CTA-pair kernel (256-row tiles over two SMs, cta_group::2) gives
-    the tiled kernel's bits on plain GEMMs: empty groups, groups of a few rows
-    (the pair's second half holding other groups' rows or nothing), N and K
+    """The CTA-pair kernel (256 weight rows on the MMA's M side over two SMs,
+    cta_group::2, and up to 256 token columns rounded to 32) gives the tiled
+    kernel's bits on plain GEMMs: empty groups, groups of a few rows (token
+    columns past the group holding other groups' rows or nothing), N and K
     not multiples of the tile."""
     g = torch.Generator(device="cuda").manual_seed(33)
     sched = build_tile_schedule(torch.tensor(sizes, device=DEV), block_m=16)
@@ -161,8 +162,9 @@ def test_pair_grouped_matmul_equals_tiled(dtype, sizes, n, k) -> None:
 
 @pytest.mark.parametrize("t", [1, 300, 1024, 4096])
 def test_pair_layer_equals_tiled(c2: LayerWeights, t: int) -> None:
-    """The whole C2 layer (SwiGLU with gate and up on the two SMs of a pair,
-    down, shared expert): the CTA-pair kernel gives the tiled kernel's bits."""
+    """The whole C2 layer (SwiGLU: each SM of a pair holds 64 gate rows and
+    the same channels' up rows, its epilogue warps exchanging halves; down;
+    shared expert): the CTA-pair kernel gives the tiled kernel's bits."""
     ws, sh = StackedExpertWeights(c2.gate, c2.up, c2.down), SharedExpertWeights(*c2.shared)
     x = randn((t, 2048), torch.Generator(device="cuda").manual_seed(950 + t), 1.0)
     for bias in (None, -1.2 * torch.log(torch.arange(64, dtype=torch.float32, device=DEV) + 1.0)):
