@@ -120,7 +120,6 @@ constexpr uint32_t kPairStageBytes = kPairWBytes + kPairXBytes;
 constexpr int kPairEpiWarps = 8;  // two per TMEM lane quarter, on alternate 32-token chunks
 constexpr int kPairThreads = 32 * (2 + kPairEpiWarps);  // warps: TMA, MMA (leader) / idle, epilogue
 constexpr int kPairTokQuant = 32;  // the MMA's token columns are a multiple of this (16 per CTA)
-constexpr int kPairTokBox = 16;    // token rows per TMA box: a CTA loads exactly its half of the columns
 constexpr uint32_t kPairEpiBytes = kPairEpiWarps * 2048;  // per epilogue warp: exchange / transpose buffer
 
 struct PairCtrl {

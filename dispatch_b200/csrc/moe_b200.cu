@@ -379,8 +379,9 @@ int run_gemm_pair(const SegSpec* specs_in, int nseg, int act_dtype, int32_t* sta
     CHECK_ARG(!spec.out_f32 && spec.k_splits == 1 && !spec.gather_rows && spec.b_dtype != MOE_DT_I8,
               "the CTA-pair kernel takes 16-bit weights, one K range, 16-bit outputs");
     spec.mma_n = 2 * moe::gemm::BM;
-    // each CTA loads 128 weight rows: 64 gate + 64 up rows, or 128 plain rows;
-    // and its half of the tile's token rows in boxes of 16
+    // each CTA loads 128 weight rows (64 gate + 64 up rows, or 128 plain rows)
+    // and its half of the tile's token rows in one 128-row box (smaller boxes,
+    // several per k-block, measured slower)
     spec.b_box_rows = spec.swiglu ? moe::gemm::BM / 2 : moe::gemm::BM;
     rc = check_seg(spec, act_dtype);
     if (rc) return rc;
